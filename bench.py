@@ -1,0 +1,456 @@
+"""Benchmark: paged decode-attention KV-read GB/s (and attention steps/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3] [--impl b200|reference]
+
+Under torchrun (N > 1) each rank owns Hkv/N KV heads (head sharding) and the
+step ends with an NCCL all-gather of the per-rank outputs.
+
+One "step" = one attention step of one layer for the whole batch at the
+configuration's context length: slot mapping -> KV append of the new token ->
+paged decode (split-K) -> split-K reduce (-> all-gather).  ``value`` times that
+step on device-resident inputs (a CUDA graph replayed K times between CUDA
+events, max over ranks); ``e2e`` times the same step through the public
+``B200AttentionBackend.decode_layer_batch`` API with host (pinned) inputs and
+outputs, as the attention node calls it.  The metric is algorithmic KV bytes
+read per step (sum_s ctx_s * Hkv * D * 2 * elem) / step time, whole job.
+
+``--impl reference`` times the CPU reference implementation (the oracle port
+of CloverInfer's CpuAttentionBackend, all host threads) on a bounded sample of
+the same workload and prints the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "paged decode-attn KV-read GB/s"
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        import torch.distributed as dist
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=__import__("datetime").timedelta(seconds=120))
+        return dist.get_rank(), world, local
+    return 0, 1, 0
+
+
+def _max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ------------------------------------------------------------------ CPU baseline
+def cpu_reference_seconds_per_step(cfg, lens, sample_seqs: int, calls: int):
+    """Time the oracle port of CpuAttentionBackend.decode_layer on a sample of
+    the workload's sequences (repeat_kv-expanded KV, as upstream requires);
+    return the extrapolated seconds for one whole-batch step."""
+    from oracle import CpuAttentionOracle, repeat_kv
+    from cloverinfer_b200.workloads import randn
+    torch.set_num_threads(os.cpu_count() or 1)
+    be = CpuAttentionOracle()
+    hq, hkv, D, dt = cfg.num_q_heads, cfg.num_kv_heads, cfg.head_dim, cfg.dtype
+    times = []
+    sample = lens[:sample_seqs]
+    for i, n in enumerate(sample):
+        k = repeat_kv(randn((n - 1, hkv, D), 100 + i, cfg.value_scale, dt), cfg.group)
+        v = repeat_kv(randn((n - 1, hkv, D), 200 + i, cfg.value_scale, dt), cfg.group)
+        be.init_request(f"s{i}", [{"key": k, "value": v}])
+    q = randn((hq, D), 1, cfg.value_scale, torch.float32)
+    kn = repeat_kv(randn((1, hkv, D), 2, cfg.value_scale, dt), cfg.group)[0]
+    vn = repeat_kv(randn((1, hkv, D), 3, cfg.value_scale, dt), cfg.group)[0]
+    for c in range(calls + 1):
+        t0 = time.perf_counter()
+        for i in range(len(sample)):
+            be.decode_layer(f"s{i}", 0, q, kn, vn, cfg.score_scale)
+        dt_s = time.perf_counter() - t0
+        if c > 0:
+            times.append(dt_s)
+        for i in range(len(sample)):  # keep the sample at the configured length
+            be._k[f"s{i}"][0] = be._k[f"s{i}"][0][:-1]
+            be._v[f"s{i}"][0] = be._v[f"s{i}"][0][:-1]
+    per_sample = statistics.median(times)
+    return per_sample * sum(lens) / sum(sample), torch.get_num_threads()
+
+
+def run_reference(args):
+    rank, world, _ = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), 0
+    if rank != 0:
+        return
+    from cloverinfer_b200.workloads import CONFIGS, context_lengths, kv_bytes
+    cfg = CONFIGS[args.config]
+    lens = context_lengths(cfg, 0)
+    nbytes = kv_bytes(lens, cfg.num_kv_heads, cfg.head_dim, cfg.dtype)
+    per_step = []
+    threads = None
+    for _ in range(args.warmup):
+        cpu_reference_seconds_per_step(cfg, lens, 1, 1)
+    for _ in range(args.steps):
+        s, threads = cpu_reference_seconds_per_step(cfg, lens, 1, 1)
+        per_step.append(s)
+    sec = statistics.median(per_step)
+    val = nbytes / sec / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": str(cfg.dtype).replace("torch.", ""), "data": "synthetic",
+        "config": {"workload": cfg.name, "batch": cfg.batch, "ctx": f"{cfg.ctx_lo}-{cfg.ctx_hi}",
+                   "num_q_heads": cfg.num_q_heads, "num_kv_heads": cfg.num_kv_heads,
+                   "head_dim": cfg.head_dim, "block_size": cfg.block_size},
+        "steps_per_s": round(1.0 / sec, 4),
+        "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": "1 of %d sequences per step (full context, repeat_kv-expanded "
+                                   "KV, decode_layer incl. the upstream cache concatenation), "
+                                   "scaled by total context" % cfg.batch},
+        "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ B200 arm
+def build_step(cfg, rank, world, lens, device, seed=0):
+    """Pool + static buffers for one decode step at the configured contexts."""
+    from cloverinfer_b200 import _lib
+    from cloverinfer_b200.head_groups import kv_head_shards
+    from cloverinfer_b200.kv_cache import PagedKVPool
+
+    lo, hi = kv_head_shards(cfg.num_kv_heads, world)[rank]
+    hkv_l = hi - lo
+    hq_l = hkv_l * cfg.group
+    B, bs, D, dt = len(lens), cfg.block_size, cfg.head_dim, cfg.dtype
+    blocks = sum(-(-n // bs) for n in lens) + 64
+    pool = PagedKVPool(blocks, bs, hkv_l, D, num_layers=1, dtype=dt, device=device,
+                       max_seqs=B, max_blocks_per_seq=max(-(-n // bs) for n in lens) + 1)
+    pool.shuffle_free_stack(1234 + seed)
+    pool.reserve(list(range(B)), list(lens))
+    g = torch.Generator(device=device).manual_seed(4321 + rank)
+    for t in (pool.k, pool.v):  # fill the whole pool: every block holds N(0,1)*scale data
+        t.normal_(0.0, cfg.value_scale, generator=g) if dt == torch.float32 else \
+            t.copy_(torch.randn(t.shape, generator=g, device=device).mul_(cfg.value_scale).to(dt))
+    q = (torch.randn((B, hq_l, D), generator=g, device=device) * cfg.value_scale).to(dt).float()
+    kn = (torch.randn((B, hkv_l, D), generator=g, device=device) * cfg.value_scale).to(dt)
+    vn = (torch.randn((B, hkv_l, D), generator=g, device=device) * cfg.value_scale).to(dt)
+    meta = torch.tensor(list(range(B)) + [n - 1 for n in lens] + list(range(B + 1)) + list(lens),
+                        dtype=torch.int32, device=device)
+    rows, pos, offs, ctx = meta[:B], meta[B:2 * B], meta[2 * B:3 * B + 1], meta[3 * B + 1:]
+    slots = torch.empty(B, dtype=torch.int64, device=device)
+    out = torch.empty_like(q)
+    nbytes = _lib.decode_workspace_bytes(B, B, 1, max(lens), hq_l, hkv_l, D, bs, dt, q.dtype,
+                                         cfg.partition_tokens)
+    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+
+    def decode_only():
+        _lib.paged_decode(out, q, pool.k[0], pool.v[0], pool.tables, offs, ctx,
+                          max_queries_per_seq=1, max_ctx_len=max(lens), score_scale=cfg.score_scale,
+                          seq_rows=rows, partition_tokens=cfg.partition_tokens, workspace=ws,
+                          status=pool.status)
+
+    def step():
+        _lib.compute_slots(pool.tables, rows, pos, offs, bs, pool.num_blocks, slots, pool.status)
+        _lib.kv_append(pool.k[0], pool.v[0], kn, vn, slots, pool.status)
+        decode_only()
+
+    return dict(pool=pool, q=q, out=out, step=step, decode_only=decode_only, hkv_local=hkv_l,
+                hq_local=hq_l, kv_range=(lo, hi))
+
+
+def run_b200(args):
+    from cloverinfer_b200 import _lib
+    from cloverinfer_b200.workloads import CONFIGS, context_lengths, kv_bytes
+
+    rank, world, local = _dist_setup()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    _lib.lib()
+    cfg = CONFIGS[args.config]
+    lens = context_lengths(cfg, 0)
+    if args.batch:
+        lens = (lens * (args.batch // len(lens) + 1))[:args.batch]
+    B = len(lens)
+    total_kv = kv_bytes(lens, cfg.num_kv_heads, cfg.head_dim, cfg.dtype)
+    st = build_step(cfg, rank, world, lens, device)
+    local_kv = kv_bytes(lens, st["hkv_local"], cfg.head_dim, cfg.dtype)
+    gather = None
+    if world > 1:
+        import torch.distributed as dist
+        recv = torch.empty((world, B, st["hq_local"], cfg.head_dim), dtype=st["out"].dtype, device=device)
+
+        def gather():
+            dist.all_gather_into_tensor(recv, st["out"])
+
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    launches_per_step = 3 + (1 if _lib.decode_workspace_bytes(
+        B, B, 1, max(lens), st["hq_local"], st["hkv_local"], cfg.head_dim, cfg.block_size,
+        cfg.dtype, torch.float32, cfg.partition_tokens) > 0 else 0)
+
+    def full_step():
+        st["step"]()
+        if gather is not None:
+            gather()
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):  # eager warm-up (module load, tensor maps, NCCL comm init)
+            full_step()
+    torch.cuda.synchronize(device)
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            full_step()
+    run = graph.replay if graph is not None else full_step
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            run()
+    torch.cuda.synchronize(device)
+    st["pool"].check_status()
+
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    clocks = ClockSampler(vis.split(",")[local] if vis else str(local))
+    clocks.start()
+    time.sleep(0.3)
+    _barrier(world)
+    torch.cuda.synchronize(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            run()
+        e1.record(stream)
+    torch.cuda.synchronize(device)
+    _barrier(world)
+    ms = e0.elapsed_time(e1) / args.steps
+    ms = _max_over_ranks(ms, world)
+
+    # Dominant kernel alone: decode (+ its split-K reduce) launches back to back
+    # in one graph, timed between CUDA events on the launching stream.
+    dec_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(dec_graph, stream=stream):
+        for _ in range(args.steps):
+            st["decode_only"]()
+    with torch.cuda.stream(stream):
+        dec_graph.replay()
+        torch.cuda.synchronize(device)
+        d0 = torch.cuda.Event(enable_timing=True)
+        d1 = torch.cuda.Event(enable_timing=True)
+        d0.record(stream)
+        dec_graph.replay()
+        d1.record(stream)
+    torch.cuda.synchronize(device)
+    dec_ms = d0.elapsed_time(d1) / args.steps
+    clk = clocks.stop()
+    st["pool"].check_status()
+    del graph, dec_graph
+
+    # ---------------- e2e through the public API (host buffers in, host out)
+    e2e = run_e2e(cfg, lens, rank, world, device, args)
+
+    hbm_peak, peak_kind = _peaks()
+    achieved = local_kv / (dec_ms * 1e-3) / 1e9
+    value = total_kv / (ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16" if cfg.dtype == torch.bfloat16 else str(cfg.dtype).replace("torch.", ""),
+        "data": "synthetic",
+        "config": {"workload": cfg.name, "batch": B, "ctx": f"{cfg.ctx_lo}-{cfg.ctx_hi}",
+                   "num_q_heads": cfg.num_q_heads, "num_kv_heads": cfg.num_kv_heads,
+                   "head_dim": cfg.head_dim, "block_size": cfg.block_size,
+                   "partition_tokens": cfg.partition_tokens,
+                   "parallelism": f"kv-head-shard{world}", "cuda_graph": graph is not None or not args.no_graph,
+                   "l2": "inputs > L2 (KV %.0f MB per GPU)" % (local_kv / 1e6)},
+        "steps_per_s": round(1e3 / ms, 2),
+        "tokens_per_s": round(B * 1e3 / ms, 2),
+        "pct_hbm_peak_per_gpu": round(100.0 * value / world / hbm_peak, 2),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "traffic": None,
+                     "kernel": "paged_decode_mma_kernel + splitk_reduce_kernel",
+                     "launch_ms": round(dec_ms, 5), "peak_kind": peak_kind},
+        "clocks": clk,
+        "gpu_launches": launches_per_step * args.steps,
+        "e2e": e2e,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sec, threads = cpu_reference_seconds_per_step(cfg, lens, 1, 2)
+        line["cpu_baseline"] = {"value": round(total_kv / sec / 1e9, 4), "unit": "GB/s",
+                                "cores": threads, "kind": "port",
+                                "sample": "1 of %d sequences, 2 timed calls (median), scaled by total "
+                                          "context; repeat_kv-expanded KV as upstream" % B}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(cfg, lens, rank, world, device, args):
+    """decode_layer_batch with per-item host tensors (pinned), as AttentionNode calls it."""
+    from cloverinfer_b200 import B200AttentionBackend, HeadShardGroup
+    from cloverinfer_b200.workloads import kv_bytes
+    shard = HeadShardGroup() if world > 1 else None
+    B, D, dt = len(lens), cfg.head_dim, cfg.dtype
+    be = B200AttentionBackend(num_blocks=sum(-(-(n + args.steps + args.warmup + 16) // cfg.block_size)
+                                             for n in lens) + 64,
+                              block_size=cfg.block_size, num_kv_heads=cfg.num_kv_heads, kv_dtype=dt,
+                              device=device, max_seqs=B, shard=shard, shuffle_seed=77,
+                              partition_tokens=cfg.partition_tokens, max_seq_len=max(lens) + 4096)
+    g = torch.Generator(device=device).manual_seed(99)
+    lo, hi = (0, cfg.num_kv_heads) if shard is None else shard.kv_range(cfg.num_kv_heads)
+    for i, n in enumerate(lens):
+        # prefill KV built on the device for speed; heads outside this rank's
+        # shard are never read, so they are left as zeros
+        k = torch.zeros((n - 1, cfg.num_kv_heads, D), dtype=dt, device=device)
+        v = torch.zeros_like(k)
+        k[:, lo:hi] = (torch.randn((n - 1, hi - lo, D), generator=g, device=device) * cfg.value_scale).to(dt)
+        v[:, lo:hi] = (torch.randn((n - 1, hi - lo, D), generator=g, device=device) * cfg.value_scale).to(dt)
+        be.init_request(f"r{i}", [{"key": k, "value": v}])
+        del k, v
+    hg = torch.Generator().manual_seed(5)
+    items = []
+    for i in range(B):
+        items.append({"request_id": f"r{i}", "layer_idx": 0,
+                      "query": torch.randn((cfg.num_q_heads, D), generator=hg).pin_memory(),
+                      "key": torch.randn((cfg.num_kv_heads, D), generator=hg).to(dt).pin_memory(),
+                      "value": torch.randn((cfg.num_kv_heads, D), generator=hg).to(dt).pin_memory(),
+                      "score_scale": cfg.score_scale})
+    h2d = sum(it["query"].numel() * 4 + 2 * it["key"].numel() * it["key"].element_size() for it in items)
+    d2h = B * cfg.num_q_heads * D * 4
+    for _ in range(args.warmup):
+        be.decode_layer_batch(items)
+    torch.cuda.synchronize(device)
+    _barrier(world)
+    lens_before = [be.get_context_len(f"r{i}") for i in range(B)]
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        be.decode_layer_batch(items)
+    e1.record()
+    torch.cuda.synchronize(device)
+    ms = _max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    # bytes actually attended over (contexts grow by one token per step)
+    attended = sum(kv_bytes([n + 1 + s for n in lens_before], cfg.num_kv_heads, D, dt)
+                   for s in range(args.steps)) / args.steps
+    for i in range(B):
+        be.free_request(f"r{i}")
+    del be
+    torch.cuda.empty_cache()
+    return {"value": round(attended / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 5),
+            "api": "B200AttentionBackend.decode_layer_batch (per-item host tensors)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c3")
+    ap.add_argument("--batch", type=int, default=0)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

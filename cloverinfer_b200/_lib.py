@@ -1,0 +1,206 @@
+"""ctypes binding of libclover_b200.so and thin tensor-level wrappers.
+
+The library is the C ABI declared in ``include/clover_b200.h``.  Loading it
+builds it in-tree first when the sources changed (nvcc, sm_100a).  There is no
+fallback: if the library cannot be built or loaded, every op raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import fcntl
+import os
+import threading
+from typing import Optional
+
+import torch
+
+from . import build as _build
+
+OK = 0
+ERR_INVALID_ARG = -1
+ERR_UNSUPPORTED = -2
+ERR_CUDA = -3
+ERR_WORKSPACE = -4
+
+DEV_BAD_SLOT = 0x1
+DEV_BAD_BLOCK = 0x2
+DEV_TABLE_FULL = 0x4
+DEV_OOM = 0x8
+DEV_TIMEOUT = 0x10
+DEV_CTX_RANGE = 0x20
+
+F32, F16, BF16 = 0, 1, 2
+_DTYPE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+
+# Every symbol include/clover_b200.h declares: name -> (restype, argtypes)
+_P = ctypes.c_void_p
+_I32 = ctypes.c_int32
+_I64 = ctypes.c_int64
+_F = ctypes.c_float
+SIGNATURES = {
+    "clover_b200_version": (ctypes.c_int, []),
+    "clover_b200_last_error": (ctypes.c_char_p, []),
+    "clover_b200_block_reserve": (ctypes.c_int, [_P, _P, _I32, _P, _I32, _P, _P, _P, _I32, _I32, _P, _P]),
+    "clover_b200_block_free": (ctypes.c_int, [_P, _P, _I32, _P, _I32, _P, _P, _I32, _P, _P]),
+    "clover_b200_compute_slots": (ctypes.c_int, [_P, _I32, _P, _P, _P, _I32, _I32, _I64, _P, _P, _P]),
+    "clover_b200_kv_append": (ctypes.c_int, [_P, _P, _P, _P, _I64, _P, _I64, _I32, _I32, _I32, _I64, _I32, _P, _P]),
+    "clover_b200_decode_workspace_bytes": (ctypes.c_int64, [_I32] * 11),
+    "clover_b200_paged_decode": (ctypes.c_int, [
+        _P, _I64, _P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _I32, _P, _P, _P,
+        _I32, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _P, _P]),
+}
+
+
+class CloverB200Error(RuntimeError):
+    """A libclover_b200 entry point returned an error code."""
+
+
+_lib: Optional[ctypes.CDLL] = None
+_lock = threading.Lock()
+
+
+def _build_locked() -> str:
+    os.makedirs(_build.OUT_DIR, exist_ok=True)
+    with open(os.path.join(_build.OUT_DIR, ".build.lock"), "w") as lk:
+        fcntl.flock(lk, fcntl.LOCK_EX)
+        try:
+            return _build.build()
+        finally:
+            fcntl.flock(lk, fcntl.LOCK_UN)
+
+
+def lib() -> ctypes.CDLL:
+    """Load (building if needed) the CUDA library; raises if impossible."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            path = _build.LIB_PATH
+            if not _build.up_to_date():
+                path = _build_locked()
+            handle = ctypes.CDLL(path)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = handle
+    return _lib
+
+
+def lib_path() -> str:
+    return _build.LIB_PATH
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != OK:
+        msg = lib().clover_b200_last_error().decode(errors="replace")
+        raise CloverB200Error(f"{what} failed ({rc}): {msg}")
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPE[dt]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dt}") from None
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("libclover_b200 ops take CUDA tensors")
+
+
+# ---------------------------------------------------------------- allocator
+def block_reserve(free_stack, free_top, tables, table_len, rows, target_tokens, block_size, status):
+    _require_cuda(free_stack, free_top, tables, table_len, rows, target_tokens, status)
+    rc = lib().clover_b200_block_reserve(
+        _ptr(free_stack), _ptr(free_top), free_stack.numel(), _ptr(tables), tables.shape[1],
+        _ptr(table_len), _ptr(rows), _ptr(target_tokens), rows.numel(), block_size,
+        _ptr(status), _stream(free_stack.device))
+    _check(rc, "clover_b200_block_reserve")
+
+
+def block_free(free_stack, free_top, tables, table_len, rows, status):
+    _require_cuda(free_stack, free_top, tables, table_len, rows, status)
+    rc = lib().clover_b200_block_free(
+        _ptr(free_stack), _ptr(free_top), free_stack.numel(), _ptr(tables), tables.shape[1],
+        _ptr(table_len), _ptr(rows), rows.numel(), _ptr(status), _stream(free_stack.device))
+    _check(rc, "clover_b200_block_free")
+
+
+def compute_slots(tables, rows, positions, token_offsets, block_size, num_blocks, slot_mapping, status):
+    _require_cuda(tables, rows, positions, token_offsets, slot_mapping, status)
+    rc = lib().clover_b200_compute_slots(
+        _ptr(tables), tables.shape[1], _ptr(rows), _ptr(positions), _ptr(token_offsets),
+        rows.numel(), block_size, num_blocks, _ptr(slot_mapping), _ptr(status),
+        _stream(tables.device))
+    _check(rc, "clover_b200_compute_slots")
+
+
+# ---------------------------------------------------------------- KV append
+def kv_append(k_cache, v_cache, k_new, v_new, slot_mapping, status):
+    """k_cache/v_cache [num_blocks, bs, H, D]; k_new/v_new [n, H, D] (token stride free)."""
+    _require_cuda(k_cache, v_cache, k_new, v_new, slot_mapping, status)
+    nb, bs, h, d = k_cache.shape
+    if k_new.dtype != k_cache.dtype or v_new.dtype != v_cache.dtype:
+        raise TypeError("kv_append: new K/V dtype must match the cache dtype")
+    if k_new.shape[1:] != (h, d) or v_new.shape != k_new.shape:
+        raise ValueError(f"kv_append: new K/V shape {tuple(k_new.shape)} != [n, {h}, {d}]")
+    if k_new.stride(2) != 1 or k_new.stride(1) != d or v_new.stride() != k_new.stride():
+        raise ValueError("kv_append: each token's [H, D] row must be contiguous")
+    rc = lib().clover_b200_kv_append(
+        _ptr(k_cache), _ptr(v_cache), _ptr(k_new), _ptr(v_new), k_new.stride(0),
+        _ptr(slot_mapping), k_new.shape[0], h, d, bs, nb, dtype_code(k_cache.dtype),
+        _ptr(status), _stream(k_cache.device))
+    _check(rc, "clover_b200_kv_append")
+
+
+# ---------------------------------------------------------------- decode
+def decode_workspace_bytes(n_seqs, n_rows, max_queries_per_seq, max_ctx_len, num_q_heads,
+                           num_kv_heads, head_dim, block_size, kv_dtype, q_dtype,
+                           partition_tokens=0) -> int:
+    nb = int(lib().clover_b200_decode_workspace_bytes(
+        n_seqs, n_rows, max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads, head_dim,
+        block_size, dtype_code(kv_dtype), dtype_code(q_dtype), partition_tokens))
+    if nb < 0:
+        raise CloverB200Error(lib().clover_b200_last_error().decode(errors="replace"))
+    return nb
+
+
+def paged_decode(out, q, k_cache, v_cache, block_tables, query_start_loc, ctx_lens, *,
+                 max_queries_per_seq, max_ctx_len, score_scale, seq_rows=None,
+                 partition_tokens=0, workspace=None, status=None):
+    """q/out [rows, Hq, D] (row stride free); caches [num_blocks, bs, Hkv, D]."""
+    _require_cuda(out, q, k_cache, v_cache, block_tables, query_start_loc, ctx_lens, seq_rows,
+                  workspace, status)
+    nb, bs, hkv, d = k_cache.shape
+    rows, hq, dq = q.shape
+    if dq != d or out.shape != q.shape:
+        raise ValueError("paged_decode: q/out shape mismatch")
+    if q.stride(2) != 1 or q.stride(1) != d or out.stride(2) != 1 or out.stride(1) != d:
+        raise ValueError("paged_decode: each row's [Hq, D] must be contiguous")
+    if out.dtype != q.dtype:
+        raise TypeError("paged_decode: out dtype must equal q dtype")
+    for t in (block_tables, query_start_loc, ctx_lens) + ((seq_rows,) if seq_rows is not None else ()):
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise TypeError("paged_decode: index tensors must be contiguous int32")
+    n_seqs = query_start_loc.numel() - 1
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    rc = lib().clover_b200_paged_decode(
+        _ptr(out), out.stride(0), _ptr(q), q.stride(0), dtype_code(q.dtype),
+        _ptr(k_cache), _ptr(v_cache), dtype_code(k_cache.dtype), nb, bs,
+        _ptr(block_tables), block_tables.stride(0), _ptr(seq_rows), _ptr(query_start_loc),
+        _ptr(ctx_lens), n_seqs, rows, max_queries_per_seq, max_ctx_len, hq, hkv, d,
+        float(score_scale), partition_tokens, _ptr(workspace), ws_bytes, _ptr(status),
+        _stream(q.device))
+    _check(rc, "clover_b200_paged_decode")

@@ -1,0 +1,328 @@
+"""B200 attention backend: drop-in for CloverInfer's AttentionNode backends.
+
+``B200AttentionBackend`` exposes the interface ``AttentionNode`` calls
+(src/core/nodes.py:88-223) — the one ``CpuAttentionBackend`` implements
+(src/core/attention_backend.py:56-144):
+
+    init_request(request_id, initial_kv, decode_reserve_tokens=0) -> int
+    decode_layer(request_id, layer_idx, query, key, value, score_scale=1.0) -> [1, Hq, D]
+    decode_layer_batch(items) -> list of [1, Hq, D]
+    get_context_len(request_id) -> int
+    free_request(request_id) -> None            (idempotent)
+    get_debug_info() -> dict
+
+with the same semantics: every call appends the new token's K/V to that
+layer's cache before attending (the token attends to itself); ``score_scale``
+is applied by the backend; ``context_len`` advances after the LAST layer
+(:120-121); unknown ids raise ``KeyError``, duplicate ids and empty
+``initial_kv`` raise ``ValueError``; outputs come back in the query's dtype
+and on the query's device.
+
+Differences that are the point of the rewrite: the KV cache is paged in HBM
+(``PagedKVPool``) with native GQA (``Hkv`` heads stored, ``repeat_kv``-expanded
+K/V accepted and collapsed); the attention is the sm_100a kernel; a batch is
+one launch sequence (reserve -> slots -> append -> decode -> reduce) instead of
+a Python loop; KV heads can be sharded over GPUs (``HeadShardGroup``) with one
+all-gather of the outputs.
+
+``decode_batch`` is the tensor API for a step-batched engine
+(src/core/scheduler.py:980-1093): ``query [T, Hq, D]``, ``key/value [T, Hkv, D]``
+for ``T = sum(n_new)`` new tokens (causal among a sequence's new tokens),
+returning ``[T, Hq, D]`` on the GPU without a host sync.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence
+
+import torch
+
+from . import _lib
+from .kv_cache import PagedKVPool, to_device_i32
+
+
+@dataclass
+class _Request:
+    row: int
+    layer_len: List[int]
+    ctx: int
+
+
+@dataclass
+class _Stats:
+    batches: int = 0
+    items: int = 0
+    tokens: int = 0
+    kv_bytes_read: int = 0
+
+
+def _default_device() -> torch.device:
+    if not torch.cuda.is_available():
+        raise RuntimeError("B200AttentionBackend requires a CUDA device (no CPU fallback)")
+    local = os.environ.get("LOCAL_RANK")
+    return torch.device("cuda", int(local) if local is not None else torch.cuda.current_device())
+
+
+class B200AttentionBackend:
+    def __init__(self, *, num_blocks: Optional[int] = None, block_size: int = 16,
+                 max_seqs: int = 256, max_seq_len: int = 131072,
+                 num_kv_heads: Optional[int] = None, kv_dtype: Optional[torch.dtype] = None,
+                 device=None, kv_cache_fraction: float = 0.5, partition_tokens: int = 0,
+                 shard=None, check_status: bool = True, shuffle_seed: Optional[int] = None,
+                 **_unused) -> None:
+        self.device = torch.device(device) if device is not None else _default_device()
+        if self.device.type != "cuda":
+            raise RuntimeError("B200AttentionBackend requires a CUDA device (no CPU fallback)")
+        _lib.lib()  # fail loudly if the CUDA library cannot be built or loaded
+        self.block_size = int(block_size)
+        self.max_seqs = int(max_seqs)
+        self.max_seq_len = int(max_seq_len)
+        self.num_blocks = num_blocks
+        self.cfg_num_kv_heads = num_kv_heads
+        self.kv_dtype = kv_dtype
+        self.kv_cache_fraction = float(kv_cache_fraction)
+        self.partition_tokens = int(partition_tokens)
+        self.shard = shard
+        self.check_status = bool(check_status)
+        self.shuffle_seed = shuffle_seed
+        self.pool: Optional[PagedKVPool] = None
+        self.num_layers = 0
+        self.num_kv_heads = 0  # total (all shards)
+        self.head_dim = 0
+        self.kv_range = (0, 0)
+        self._reqs: Dict[str, _Request] = {}
+        self.stats = _Stats()
+
+    # ------------------------------------------------------------ setup
+    def _ensure_pool(self, num_layers: int, heads: int, head_dim: int, dtype: torch.dtype) -> None:
+        if self.pool is not None:
+            if (num_layers, head_dim) != (self.num_layers, self.head_dim):
+                raise ValueError(
+                    f"initial_kv has {num_layers} layers x head_dim {head_dim}; backend holds "
+                    f"{self.num_layers} x {self.head_dim}")
+            return
+        hkv = int(self.cfg_num_kv_heads or heads)
+        if heads % hkv:
+            raise ValueError(f"initial_kv has {heads} heads, not a multiple of num_kv_heads={hkv}")
+        dt = self.kv_dtype or dtype
+        if dt not in (torch.float32, torch.float16, torch.bfloat16):
+            raise TypeError(f"unsupported KV dtype {dt}")
+        self.num_layers, self.num_kv_heads, self.head_dim, self.kv_dtype = num_layers, hkv, head_dim, dt
+        if self.shard is not None:
+            self.kv_range = self.shard.kv_range(hkv)
+        else:
+            self.kv_range = (0, hkv)
+        local = self.kv_range[1] - self.kv_range[0]
+        nb = self.num_blocks
+        esz = torch.empty((), dtype=dt).element_size()
+        per_block = 2 * num_layers * self.block_size * local * head_dim * esz
+        if nb is None:
+            free, _ = torch.cuda.mem_get_info(self.device)
+            nb = max(16, int(free * self.kv_cache_fraction) // per_block)
+        width = min(nb, -(-self.max_seq_len // self.block_size) + 1)
+        self.pool = PagedKVPool(nb, self.block_size, local, head_dim, num_layers=num_layers,
+                                dtype=dt, device=self.device, max_seqs=self.max_seqs,
+                                max_blocks_per_seq=width)
+        if self.shuffle_seed is not None:
+            self.pool.shuffle_free_stack(self.shuffle_seed)
+
+    def _local_kv(self, x: torch.Tensor) -> torch.Tensor:
+        """[T, H, D] on device in the cache dtype, local KV heads only.  H may be
+        Hkv (native) or Hq = Hkv * g (repeat_kv-expanded: one head per group kept)."""
+        h = x.shape[1]
+        if h != self.num_kv_heads:
+            if h % self.num_kv_heads:
+                raise ValueError(f"K/V has {h} heads; expected {self.num_kv_heads} (or a multiple)")
+            x = x[:, :: h // self.num_kv_heads]
+        lo, hi = self.kv_range
+        if (lo, hi) != (0, self.num_kv_heads):
+            x = x[:, lo:hi]
+        return x.to(device=self.device, dtype=self.kv_dtype, non_blocking=True).contiguous()
+
+    # ------------------------------------------------------------ interface
+    def init_request(self, request_id: str, initial_kv: List[Dict[str, torch.Tensor]],
+                     decode_reserve_tokens: int = 0) -> int:
+        if request_id in self._reqs:
+            raise ValueError(f"Request {request_id} already exists")
+        if not initial_kv:
+            raise ValueError("initial_kv must contain at least one layer")
+        k0 = initial_kv[0]["key"]
+        if k0.dim() != 3:
+            raise ValueError(f"initial_kv key must be [T, H, D], got {tuple(k0.shape)}")
+        T, H, D = (int(s) for s in k0.shape)
+        for layer in initial_kv:
+            if tuple(layer["key"].shape) != (T, H, D) or tuple(layer["value"].shape) != (T, H, D):
+                raise ValueError("all initial_kv layers must share one [T, H, D] shape")
+        self._ensure_pool(len(initial_kv), H, D, k0.dtype)
+        pool = self.pool
+        row = pool.acquire_row()
+        try:
+            pool.reserve([row], [T + max(1, int(decode_reserve_tokens))], "OOM: Not enough blocks")
+        except Exception:
+            pool._free_rows.append(row)
+            raise
+        if T > 0:
+            dev = self.device
+            meta = to_device_i32([row, 0, 0, T], dev)
+            slots = pool.slots(meta[0:1], meta[1:2], meta[2:4], T)
+            for li, layer in enumerate(initial_kv):
+                pool.append(li, self._local_kv(layer["key"]), self._local_kv(layer["value"]), slots)
+        self._reqs[request_id] = _Request(row=row, layer_len=[T] * self.num_layers, ctx=T)
+        return T
+
+    def get_context_len(self, request_id: str) -> int:
+        return self._reqs[request_id].ctx
+
+    def free_request(self, request_id: str) -> None:
+        req = self._reqs.pop(request_id, None)
+        if req is not None:
+            self.pool.release_row(req.row)
+
+    def decode_layer(self, request_id: str, layer_idx: int, query: torch.Tensor,
+                     key: torch.Tensor, value: torch.Tensor, score_scale: float = 1.0) -> torch.Tensor:
+        return self.decode_layer_batch([{"request_id": request_id, "layer_idx": layer_idx,
+                                         "query": query, "key": key, "value": value,
+                                         "score_scale": score_scale}])[0]
+
+    def decode_layer_batch(self, items: List[Dict[str, object]]) -> List[torch.Tensor]:
+        results: List[Optional[torch.Tensor]] = [None] * len(items)
+        i = 0
+        while i < len(items):
+            layer = int(items[i]["layer_idx"])
+            scale = float(items[i].get("score_scale", 1.0))
+            seen = set()
+            j = i
+            while j < len(items):
+                it = items[j]
+                rid = str(it["request_id"])
+                if (int(it["layer_idx"]) != layer or float(it.get("score_scale", 1.0)) != scale
+                        or rid in seen):
+                    break
+                seen.add(rid)
+                j += 1
+            self._run_items(items[i:j], layer, scale, results, i)
+            i = j
+        return results  # type: ignore[return-value]
+
+    def _run_items(self, items, layer: int, scale: float, results, base: int) -> None:
+        rids = [str(it["request_id"]) for it in items]
+        for r in rids:
+            if r not in self._reqs:
+                raise KeyError(f"Unknown request {r}")
+        qs = [it["query"] for it in items]
+        q_dtype = qs[0].dtype
+        on_host = not qs[0].is_cuda
+        sq = lambda t: t.squeeze(0) if t.dim() == 3 else t  # noqa: E731
+        if on_host:
+            q = torch.stack([sq(t) for t in qs]).pin_memory().to(self.device, non_blocking=True)
+            k = torch.stack([sq(it["key"]) for it in items]).pin_memory()
+            v = torch.stack([sq(it["value"]) for it in items]).pin_memory()
+        else:
+            q = torch.stack([sq(t) for t in qs])
+            k = torch.stack([sq(it["key"]) for it in items])
+            v = torch.stack([sq(it["value"]) for it in items])
+        out = self.decode_batch(rids, layer, q, k, v, scale)
+        if on_host:
+            out = out.to("cpu")
+        if out.dtype != q_dtype:
+            out = out.to(q_dtype)
+        if self.check_status and on_host:
+            self.pool.check_status()
+        for n in range(len(items)):
+            results[base + n] = out[n:n + 1]
+
+    # ------------------------------------------------------------ tensor API
+    def decode_batch(self, request_ids: Sequence[str], layer_idx: int, query: torch.Tensor,
+                     key: torch.Tensor, value: torch.Tensor, score_scale: float = 1.0,
+                     n_new: Optional[Sequence[int]] = None) -> torch.Tensor:
+        """Append ``n_new[b]`` tokens per request and attend causally.
+
+        query [T, Hq, D] (fp32, or the cache dtype), key/value [T, Hkv or Hq, D];
+        returns [T, Hq, D] on the GPU in the query dtype (all heads: sharded
+        backends all-gather).  Enqueued on the current stream; no host sync.
+        """
+        pool = self.pool
+        if pool is None:
+            raise KeyError("no request has been initialised")
+        B = len(request_ids)
+        n_new = [1] * B if n_new is None else [int(n) for n in n_new]
+        T = sum(n_new)
+        if query.shape[0] != T or key.shape[0] != T or value.shape[0] != T:
+            raise ValueError(f"expected {T} new tokens, got q {tuple(query.shape)} k {tuple(key.shape)}")
+        reqs = []
+        for r in request_ids:
+            try:
+                reqs.append(self._reqs[r])
+            except KeyError:
+                raise KeyError(f"Unknown request {r}") from None
+        if not 0 <= layer_idx < self.num_layers:
+            raise IndexError(f"layer_idx {layer_idx} out of range [0, {self.num_layers})")
+        hq = query.shape[1]
+        if hq % self.num_kv_heads or query.shape[2] != self.head_dim:
+            raise ValueError(f"query {tuple(query.shape)} does not fit {self.num_kv_heads} KV heads x {self.head_dim}")
+        group = hq // self.num_kv_heads
+        rows = [r.row for r in reqs]
+        pos = [r.layer_len[layer_idx] for r in reqs]
+        targets = [p + n for p, n in zip(pos, n_new)]
+        pool.reserve(rows, targets, "OOM during append")
+
+        offs = [0]
+        ctx_rows: List[int] = []
+        for p, n in zip(pos, n_new):
+            offs.append(offs[-1] + n)
+            ctx_rows.extend(range(p + 1, p + n + 1))
+        meta = to_device_i32(rows + pos + offs + ctx_rows, self.device)
+        rows_d, pos_d = meta[0:B], meta[B:2 * B]
+        offs_d, ctx_d = meta[2 * B:3 * B + 1], meta[3 * B + 1:]
+
+        slots = pool.slots(rows_d, pos_d, offs_d, T)
+        pool.append(layer_idx, self._local_kv(key), self._local_kv(value), slots)
+
+        lo, hi = self.kv_range
+        q = query.to(self.device, non_blocking=True)
+        if q.dtype not in (torch.float32, self.kv_dtype):
+            q = q.float()
+        if (lo, hi) != (0, self.num_kv_heads):
+            q = q[:, lo * group:hi * group]
+        if q.stride(2) != 1 or q.stride(1) != self.head_dim:
+            q = q.contiguous()
+        out = pool.decode(layer_idx, q, offs_d, ctx_d, rows_d, max(n_new), max(targets),
+                          score_scale, partition_tokens=self.partition_tokens)
+        for r, n in zip(reqs, n_new):
+            r.layer_len[layer_idx] += n
+            if layer_idx == self.num_layers - 1:
+                r.ctx += n
+        st = self.stats
+        st.batches += 1
+        st.items += B
+        st.tokens += T
+        esz = torch.empty((), dtype=self.kv_dtype).element_size()
+        st.kv_bytes_read += sum(targets) * (hi - lo) * self.head_dim * 2 * esz
+        if self.shard is not None and self.shard.world > 1:
+            out = self.shard.gather(out, self.num_kv_heads, group)
+        return out
+
+    # ------------------------------------------------------------ debug
+    def get_debug_info(self) -> dict:
+        pool = self.pool
+        info = {
+            "backend": "b200",
+            "library": _lib.lib_path(),
+            "device": str(self.device),
+            "live_requests": len(self._reqs),
+            "stats": dict(self.stats.__dict__),
+        }
+        if pool is not None:
+            info.update({
+                "num_layers": self.num_layers, "num_kv_heads": self.num_kv_heads,
+                "kv_heads_local": list(self.kv_range), "head_dim": self.head_dim,
+                "kv_dtype": str(self.kv_dtype), "block_size": pool.block_size,
+                "num_blocks": pool.num_blocks, "free_blocks": pool.free_count,
+                "kv_cache_bytes": 2 * pool.k.numel() * pool.k.element_size(),
+            })
+        if self.shard is not None:
+            info["shard"] = {"rank": self.shard.rank, "world": self.shard.world}
+        return info

@@ -1,0 +1,872 @@
+// Paged decode attention for B200 (sm_100a): GQA, causal multi-token rows,
+// split-K flash-decoding and the split-K reduce.
+//
+// Computes, for every query row r and query head h (KV head h / group):
+//     out[r,h,:] = softmax(score_scale * q[r,h,:] . K[0:ctx_r]^T) . V[0:ctx_r]
+// over a paged cache `[num_blocks, block_size, num_kv_heads, head_dim]` —
+// the math of CpuAttentionBackend.decode_layer (src/core/attention_backend.py:113-118)
+// and of KVCacheManager.attention / paged_attention
+// (src/core/memory_manager.py:175-239, src/kernels/csrc/attention.cu:16-115),
+// with the scale passed in instead of fixed at 1/sqrt(D).
+//
+// Work decomposition: one CTA per (partition p, KV head, column chunk, sequence).
+// A "column" is one (query row of the sequence, query head of the KV head's group)
+// pair; a chunk holds up to 8 columns, so all query heads that share a KV head —
+// and all new tokens of a multi-token step — read each KV block from HBM once.
+//
+// Tensor-core path (bf16/fp16 cache, head_dim 64/128/256, block 16/32):
+//   * each warp owns a private ring of STAGES slots; lane 0 fetches a whole
+//     KV block (K and V tiles, `block_size x head_dim`) of its KV head with
+//     3-D TMA tiled loads (128-byte swizzle) completing on an mbarrier;
+//   * S^T-free orientation: S[tokens x cols] = K . Q^T with mma.sync m16n8k16
+//     (tokens = M, columns = N = 8), fp32 accumulate; fp32 queries are split
+//     hi + lo into two 16-bit operands so scores keep ~fp32 accuracy;
+//   * online softmax in the base-2 domain on the accumulator fragment;
+//   * O^T[dims x cols] += V^T . P^T: V^T fragments come from ldmatrix.trans,
+//     P^T from movmatrix.trans of the score fragment, P split hi + lo;
+//   * warps merge their (m, l, O) in shared memory; a single-partition row is
+//     written directly, otherwise (O/l, m + log2 l) goes to the workspace and
+//     splitk_reduce_kernel combines partitions.
+// SIMT path (fp32 cache or other shapes): same decomposition and workspace
+// format with CUDA-core dot products.
+#include <math.h>
+#include <mutex>
+
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace clover {
+
+constexpr int kNumWarps = 4;
+constexpr int kThreads = kNumWarps * 32;
+constexpr int kMmaCols = 8;
+
+struct DecodeArgs {
+  void* out;
+  int64_t out_stride;
+  const void* q;
+  int64_t q_stride;
+  int32_t q_dtype;
+  const void* k_cache;
+  const void* v_cache;
+  const int32_t* tables;
+  int32_t table_stride;
+  const int32_t* seq_rows;
+  const int32_t* qsl;
+  const int32_t* ctx;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t group;
+  int32_t block_size;
+  int64_t num_blocks;
+  float scale_log2;
+  int32_t part_tokens;
+  int32_t max_parts;
+  int32_t cols_per_cta;
+  int32_t col_chunks;
+  float* part_out;
+  float* part_lse;
+  int32_t* status;
+};
+
+struct ColInfo {
+  int32_t qrow, qhead, limit;
+  bool valid;
+};
+
+__device__ __forceinline__ ColInfo col_info(const DecodeArgs& a, int row0, int nq, int kvh,
+                                            int cglob) {
+  ColInfo c{0, 0, 0, false};
+  if (cglob < nq * a.group) {
+    const int j = cglob / a.group;
+    c.qrow = row0 + j;
+    c.qhead = kvh * a.group + (cglob - j * a.group);
+    c.limit = __ldg(a.ctx + c.qrow);
+    c.valid = true;
+  }
+  return c;
+}
+
+__device__ __forceinline__ float load_q(const DecodeArgs& a, int64_t idx) {
+  switch (a.q_dtype) {
+    case CLOVER_B200_F32: return __ldg(static_cast<const float*>(a.q) + idx);
+    case CLOVER_B200_F16: return __half2float(static_cast<const __half*>(a.q)[idx]);
+    default: return __bfloat162float(static_cast<const __nv_bfloat16*>(a.q)[idx]);
+  }
+}
+
+__device__ __forceinline__ void store_out(const DecodeArgs& a, int64_t idx, float v) {
+  switch (a.q_dtype) {
+    case CLOVER_B200_F32: static_cast<float*>(a.out)[idx] = v; break;
+    case CLOVER_B200_F16: static_cast<__half*>(a.out)[idx] = __float2half_rn(v); break;
+    default: static_cast<__nv_bfloat16*>(a.out)[idx] = __float2bfloat16_rn(v); break;
+  }
+}
+
+// Common CTA prologue: the token range this CTA owns.  Returns false if the
+// CTA has no work.
+struct CtaWork {
+  int b, p, kvh, chunk, row0, nq, tok_begin, tok_end;
+  const int32_t* tab;
+};
+
+// Columns whose context is empty attend to nothing: their output is zero.
+__device__ __forceinline__ void zero_empty_columns(const DecodeArgs& a, const CtaWork& w, int D) {
+  for (int idx = threadIdx.x; idx < a.cols_per_cta * D; idx += kThreads) {
+    const int col = idx / D;
+    const ColInfo ci = col_info(a, w.row0, w.nq, w.kvh, w.chunk * a.cols_per_cta + col);
+    if (ci.valid && ci.limit <= 0)
+      store_out(a, (int64_t)ci.qrow * a.out_stride + (int64_t)ci.qhead * D + (idx - col * D), 0.f);
+  }
+}
+
+__device__ __forceinline__ bool cta_work(const DecodeArgs& a, CtaWork& w, int D) {
+  // After a bounded wait gave up anywhere, later CTAs stop at once.
+  if (a.status != nullptr && (*(volatile int32_t*)a.status & CLOVER_B200_DEV_TIMEOUT)) return false;
+  w.b = blockIdx.z;
+  w.p = blockIdx.x;
+  w.kvh = blockIdx.y / a.col_chunks;
+  w.chunk = blockIdx.y - w.kvh * a.col_chunks;
+  w.row0 = __ldg(a.qsl + w.b);
+  w.nq = __ldg(a.qsl + w.b + 1) - w.row0;
+  const int c0 = w.chunk * a.cols_per_cta;
+  if (w.nq <= 0 || c0 >= w.nq * a.group) return false;
+  // The longest causal limit among this chunk's rows bounds the token range.
+  const int j_lo = c0 / a.group;
+  const int j_hi = min(w.nq - 1, (c0 + a.cols_per_cta - 1) / a.group);
+  int ctx_end = 0;
+  for (int j = j_lo; j <= j_hi; ++j) ctx_end = max(ctx_end, __ldg(a.ctx + w.row0 + j));
+  if (ctx_end > a.max_parts * a.part_tokens) {
+    if (threadIdx.x == 0 && w.p == 0 && w.kvh == 0) raise_status(a.status, CLOVER_B200_DEV_CTX_RANGE);
+    ctx_end = a.max_parts * a.part_tokens;
+  }
+  w.tok_begin = w.p * a.part_tokens;
+  if (w.tok_begin >= ctx_end) {
+    if (w.p == 0) zero_empty_columns(a, w, D);
+    return false;
+  }
+  w.tok_end = min(w.tok_begin + a.part_tokens, ctx_end);
+  const int trow = a.seq_rows ? __ldg(a.seq_rows + w.b) : w.b;
+  w.tab = a.tables + (int64_t)trow * a.table_stride;
+  return true;
+}
+
+// Merge per-warp (m, l, O) partial states held in shared memory and store
+// either the final output (single-partition rows) or the split-K partial.
+// red_acc: [kNumWarps][cols][D+4], red_m/red_l: [kNumWarps][cols].
+__device__ __forceinline__ void merge_store_rt(const DecodeArgs& a, const CtaWork& w,
+                                               const float* red_acc, const float* red_m,
+                                               const float* red_l, int cols, int D) {
+  for (int idx = threadIdx.x; idx < cols * D; idx += kThreads) {
+    const int col = idx / D;
+    const int dim = idx - col * D;
+    const ColInfo ci = col_info(a, w.row0, w.nq, w.kvh, w.chunk * a.cols_per_cta + col);
+    if (!ci.valid) continue;
+    if (ci.limit <= w.tok_begin) {
+      if (w.p == 0) store_out(a, (int64_t)ci.qrow * a.out_stride + (int64_t)ci.qhead * D + dim, 0.f);
+      continue;
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < kNumWarps; ++k) M = fmaxf(M, red_m[k * cols + col]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int k = 0; k < kNumWarps; ++k) {
+        const float e = fast_exp2(red_m[k * cols + col] - M);
+        L += red_l[k * cols + col] * e;
+        O += red_acc[(k * cols + col) * (D + 4) + dim] * e;
+      }
+    }
+    const float o = L > 0.f ? O / L : 0.f;
+    const int nparts = (ci.limit + a.part_tokens - 1) / a.part_tokens;
+    if (nparts == 1) {
+      store_out(a, (int64_t)ci.qrow * a.out_stride + (int64_t)ci.qhead * D + dim, o);
+    } else {
+      const int64_t base = ((int64_t)ci.qrow * a.num_q_heads + ci.qhead) * a.max_parts + w.p;
+      a.part_out[base * D + dim] = o;
+      if (dim == 0) a.part_lse[base] = L > 0.f ? M + fast_log2(L) : -INFINITY;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ tensor-core path
+template <int D, int BS>
+struct MmaGeom {
+  static constexpr int kChunks = D / 64;          // 128-byte swizzle atoms per row
+  static constexpr int kTile = BS * D * 2;        // bytes of one K (or V) tile
+  static constexpr int kStage = 2 * kTile;        // K + V
+  static constexpr int kStages = (D >= 256) ? 2 : 3;
+  static constexpr int kPipeBytes = kNumWarps * kStages * kStage;
+  static constexpr int kRedBytes = kNumWarps * kMmaCols * (D + 4) * 4 + 2 * kNumWarps * kMmaCols * 4;
+  static constexpr int kSmem = (kPipeBytes > kRedBytes ? kPipeBytes : kRedBytes) + 1024;
+  static constexpr int kMaxBlocksPerCta = 32 * kNumWarps;  // one table id per lane per warp
+};
+
+// byte offset of 16-byte chunk `cg` (along head_dim) of tile row `r` (128B swizzle)
+template <int BS>
+__device__ __forceinline__ uint32_t swz(int r, int cg) {
+  const int c64 = cg >> 3, c = cg & 7;
+  return (uint32_t)(c64 * BS * 128 + r * 128 + ((c ^ (r & 7)) << 4));
+}
+
+template <typename T, bool QF32, int D, int BS>
+__global__ void __launch_bounds__(kThreads, 2)
+paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const DecodeArgs a) {
+  using G = MmaGeom<D, BS>;
+  constexpr int STAGES = G::kStages;
+  constexpr int MT = BS / 16;  // token m-tiles per block
+  constexpr int KK = D / 16;   // k-steps (QK) / m-tiles (PV) over head_dim
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[kNumWarps * STAGES];
+  __shared__ int s_abort;
+
+  CtaWork w;
+  if (!cta_work(a, w, D)) return;
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kNumWarps * STAGES; ++i) mbar_init(smem_addr(&bars[i]), 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    s_abort = 0;
+  }
+  __syncthreads();
+
+  const int blk0 = w.tok_begin / BS;
+  const int n_blk = (w.tok_end - w.tok_begin + BS - 1) / BS;
+  const int n_mine = warp < n_blk ? (n_blk - warp + kNumWarps - 1) / kNumWarps : 0;
+  int my_blk = 0;
+  if (lane < n_mine) {
+    const int bi = blk0 + warp + lane * kNumWarps;
+    int id = bi < a.table_stride ? __ldg(w.tab + bi) : -1;
+    if (id < 0 || id >= a.num_blocks) {
+      raise_status(a.status, CLOVER_B200_DEV_BAD_BLOCK);
+      id = 0;  // keep the pipeline well-formed; the output is flagged invalid
+    }
+    my_blk = id;
+  }
+  const uint32_t ring = smem_addr(smem) + warp * STAGES * G::kStage;
+  const uint32_t bar0 = smem_addr(&bars[warp * STAGES]);
+
+  auto issue = [&](int k) {
+    const int id = __shfl_sync(0xffffffffu, my_blk, k);
+    if (lane == 0) {
+      const int s = k % STAGES;
+      const uint32_t bar = bar0 + s * 8;
+      const uint32_t kd = ring + s * G::kStage;
+      const uint32_t vd = kd + G::kTile;
+      mbar_arrive_expect_tx(bar, G::kStage);
+#pragma unroll
+      for (int c = 0; c < G::kChunks; ++c) {
+        tma_load_3d(kd + c * BS * 128, &tmK, c * 64, w.kvh, id * BS, bar);
+        tma_load_3d(vd + c * BS * 128, &tmV, c * 64, w.kvh, id * BS, bar);
+      }
+    }
+  };
+
+  // Query fragments (MMA B operand, columns = lane / 4).
+  uint32_t qh[KK][2], ql[KK][2];
+  {
+    const ColInfo ci = col_info(a, w.row0, w.nq, w.kvh, w.chunk * kMmaCols + (lane >> 2));
+    const int64_t qbase = (int64_t)ci.qrow * a.q_stride + (int64_t)ci.qhead * D;
+#pragma unroll
+    for (int kk = 0; kk < KK; ++kk) {
+      const int d0 = kk * 16 + (lane & 3) * 2;
+      float x0 = 0.f, x1 = 0.f, x8 = 0.f, x9 = 0.f;
+      if (ci.valid) {
+        x0 = load_q(a, qbase + d0);
+        x1 = load_q(a, qbase + d0 + 1);
+        x8 = load_q(a, qbase + d0 + 8);
+        x9 = load_q(a, qbase + d0 + 9);
+      }
+      if (QF32) {
+        split_pack<T>(x0, x1, qh[kk][0], ql[kk][0]);
+        split_pack<T>(x8, x9, qh[kk][1], ql[kk][1]);
+      } else {
+        qh[kk][0] = Pack<T>::pack(x0, x1);
+        qh[kk][1] = Pack<T>::pack(x8, x9);
+      }
+    }
+  }
+  // Causal limits of this thread's two accumulator columns.
+  const int ca = (lane & 3) * 2;
+  int lim_a, lim_b;
+  {
+    const ColInfo c0 = col_info(a, w.row0, w.nq, w.kvh, w.chunk * kMmaCols + ca);
+    const ColInfo c1 = col_info(a, w.row0, w.nq, w.kvh, w.chunk * kMmaCols + ca + 1);
+    lim_a = c0.valid ? c0.limit : 0;
+    lim_b = c1.valid ? c1.limit : 0;
+  }
+
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+  float acc[KK][4];
+#pragma unroll
+  for (int i = 0; i < KK; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+
+  const int npre = n_mine < STAGES ? n_mine : STAGES;
+  for (int k = 0; k < npre; ++k) issue(k);
+  int issued = npre;
+  int consumed = 0;
+  bool timed_out = false;
+
+  for (int k = 0; k < n_mine; ++k) {
+    const int s = k % STAGES;
+    if (!mbar_wait_bounded(bar0 + s * 8, (k / STAGES) & 1, kWaitLimitNs)) {
+      timed_out = true;
+      break;
+    }
+    consumed = k + 1;
+    const uint32_t ks = ring + s * G::kStage;
+    const uint32_t vs = ks + G::kTile;
+    const int tok0 = (blk0 + warp + k * kNumWarps) * BS;
+    const int nvalid = w.tok_end - tok0;
+    if (nvalid < BS) {
+      // Rows past the end of the context may hold stale data: zero them in V
+      // so that P = 0 never multiplies a non-finite value.
+      uint8_t* vg = smem + (vs - smem_addr(smem));
+      for (int idx = lane; idx < (BS - nvalid) * (D / 8); idx += 32) {
+        const int r = nvalid + idx / (D / 8);
+        const int cg = idx % (D / 8);
+        *reinterpret_cast<uint4*>(vg + swz<BS>(r, cg)) = make_uint4(0, 0, 0, 0);
+      }
+      __syncwarp();
+    }
+
+    // ---- S = K . Q^T (tokens x columns), fp32 accumulate
+    float sc[MT][4];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.f;
+      const int r = mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int kk = 0; kk < KK; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(ks + swz<BS>(r, kk * 2 + (lane >> 4)), a0, a1, a2, a3);
+        MmaOp<T>::run(sc[mt], a0, a1, a2, a3, qh[kk][0], qh[kk][1]);
+        if (QF32) MmaOp<T>::run(sc[mt], a0, a1, a2, a3, ql[kk][0], ql[kk][1]);
+      }
+    }
+    // ---- scale (base-2 domain), causal mask, block max per column
+    float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int t = tok0 + mt * 16 + (lane >> 2) + h * 8;
+        const float sa = t < lim_a ? sc[mt][2 * h] * a.scale_log2 : -INFINITY;
+        const float sb = t < lim_b ? sc[mt][2 * h + 1] * a.scale_log2 : -INFINITY;
+        sc[mt][2 * h] = sa;
+        sc[mt][2 * h + 1] = sb;
+        mx_a = fmaxf(mx_a, sa);
+        mx_b = fmaxf(mx_b, sb);
+      }
+    }
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, off));
+      mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, off));
+    }
+    const float nm_a = fmaxf(m_a, mx_a), nm_b = fmaxf(m_b, mx_b);
+    const float u_a = nm_a == -INFINITY ? 0.f : nm_a;
+    const float u_b = nm_b == -INFINITY ? 0.f : nm_b;
+    const float al_a = fast_exp2(m_a - u_a), al_b = fast_exp2(m_b - u_b);
+    m_a = nm_a;
+    m_b = nm_b;
+    l_a *= al_a;
+    l_b *= al_b;
+#pragma unroll
+    for (int i = 0; i < KK; ++i) {
+      acc[i][0] *= al_a;
+      acc[i][1] *= al_b;
+      acc[i][2] *= al_a;
+      acc[i][3] *= al_b;
+    }
+    // ---- O^T += V^T . P^T
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const float p0 = fast_exp2(sc[mt][0] - u_a), p1 = fast_exp2(sc[mt][1] - u_b);
+      const float p2 = fast_exp2(sc[mt][2] - u_a), p3 = fast_exp2(sc[mt][3] - u_b);
+      l_a += p0 + p2;
+      l_b += p1 + p3;
+      uint32_t h_top, l_top, h_bot, l_bot;
+      split_pack<T>(p0, p1, h_top, l_top);
+      split_pack<T>(p2, p3, h_bot, l_bot);
+      const uint32_t bh0 = movm_trans(h_top), bh1 = movm_trans(h_bot);
+      const uint32_t bl0 = movm_trans(l_top), bl1 = movm_trans(l_bot);
+      const int grp = lane >> 3;
+      const int r = mt * 16 + (lane & 7) + (grp >> 1) * 8;
+#pragma unroll
+      for (int dm = 0; dm < KK; ++dm) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_trans(vs + swz<BS>(r, dm * 2 + (grp & 1)), a0, a1, a2, a3);
+        MmaOp<T>::run(acc[dm], a0, a1, a2, a3, bh0, bh1);
+        MmaOp<T>::run(acc[dm], a0, a1, a2, a3, bl0, bl1);
+      }
+    }
+    __syncwarp();
+    if (k + STAGES < n_mine) {
+      issue(k + STAGES);
+      ++issued;
+    }
+  }
+
+  if (timed_out) {
+    // Drain this warp's copies still in flight (bounded) before giving up.
+    for (int k = consumed; k < issued; ++k)
+      mbar_wait_bounded(bar0 + (k % STAGES) * 8, (k / STAGES) & 1, kWaitLimitNs);
+    if (lane == 0) {
+      raise_status(a.status, CLOVER_B200_DEV_TIMEOUT);
+      atomicExch(&s_abort, 1);
+    }
+  }
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, off);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, off);
+  }
+  __syncthreads();  // every warp is done with its ring: reuse it for the merge
+  if (s_abort) return;
+
+  float* red_acc = reinterpret_cast<float*>(smem);
+  float* red_m = red_acc + kNumWarps * kMmaCols * (D + 4);
+  float* red_l = red_m + kNumWarps * kMmaCols;
+  {
+    float* base = red_acc + (warp * kMmaCols) * (D + 4);
+#pragma unroll
+    for (int dm = 0; dm < KK; ++dm) {
+      const int d = dm * 16 + (lane >> 2);
+      base[ca * (D + 4) + d] = acc[dm][0];
+      base[(ca + 1) * (D + 4) + d] = acc[dm][1];
+      base[ca * (D + 4) + d + 8] = acc[dm][2];
+      base[(ca + 1) * (D + 4) + d + 8] = acc[dm][3];
+    }
+    if (lane < 4) {
+      red_m[warp * kMmaCols + ca] = m_a;
+      red_m[warp * kMmaCols + ca + 1] = m_b;
+      red_l[warp * kMmaCols + ca] = l_a;
+      red_l[warp * kMmaCols + ca + 1] = l_b;
+    }
+  }
+  __syncthreads();
+  merge_store_rt(a, w, red_acc, red_m, red_l, kMmaCols, D);
+}
+
+// ------------------------------------------------------------------ SIMT path
+// Any head_dim <= 32 * EPL: lane l holds dims [l*EPL, l*EPL + EPL) of a token row.
+template <typename KT, int EPL, int NC>
+__global__ void __launch_bounds__(kThreads)
+paged_decode_simt_kernel(const DecodeArgs a, int D) {
+  constexpr int DMAX = 32 * EPL;
+  __shared__ float red_acc[kNumWarps * NC * (DMAX + 4)];
+  __shared__ float red_m[kNumWarps * NC], red_l[kNumWarps * NC];
+  CtaWork w;
+  if (!cta_work(a, w, D)) return;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int d0 = lane * EPL;
+
+  float qv[NC][EPL];
+  int lim[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const ColInfo ci = col_info(a, w.row0, w.nq, w.kvh, w.chunk * NC + c);
+    lim[c] = ci.valid ? ci.limit : 0;
+    const int64_t qb = (int64_t)ci.qrow * a.q_stride + (int64_t)ci.qhead * D + d0;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e)
+      qv[c][e] = (ci.valid && d0 + e < D) ? load_q(a, qb + e) * a.scale_log2 : 0.f;
+  }
+  float m[NC], l[NC], acc[NC][EPL];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    m[c] = -INFINITY;
+    l[c] = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[c][e] = 0.f;
+  }
+  const KT* kc = static_cast<const KT*>(a.k_cache);
+  const KT* vc = static_cast<const KT*>(a.v_cache);
+  const int BS = a.block_size;
+  for (int t = w.tok_begin + warp; t < w.tok_end; t += kNumWarps) {
+    const int bi = t / BS;
+    int blk = bi < a.table_stride ? __ldg(w.tab + bi) : -1;
+    if (blk < 0 || blk >= a.num_blocks) {
+      if (lane == 0) raise_status(a.status, CLOVER_B200_DEV_BAD_BLOCK);
+      blk = 0;
+    }
+    const int64_t row = (((int64_t)blk * BS + (t - bi * BS)) * a.num_kv_heads + w.kvh) * D + d0;
+    float kx[EPL], vx[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+      const bool in = d0 + e < D;
+      kx[e] = in ? load_f<KT>(kc + row + e) : 0.f;
+      vx[e] = in ? load_f<KT>(vc + row + e) : 0.f;
+    }
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) s = fmaf(qv[c][e], kx[e], s);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+      s = t < lim[c] ? s : -INFINITY;
+      const float nm = fmaxf(m[c], s);
+      const float u = nm == -INFINITY ? 0.f : nm;
+      const float al = fast_exp2(m[c] - u);
+      const float pe = fast_exp2(s - u);
+      m[c] = nm;
+      l[c] = l[c] * al + pe;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) acc[c][e] = fmaf(pe, vx[e], acc[c][e] * al);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e)
+      if (d0 + e < D) red_acc[(warp * NC + c) * (D + 4) + d0 + e] = acc[c][e];
+    if (lane == 0) {
+      red_m[warp * NC + c] = m[c];
+      red_l[warp * NC + c] = l[c];
+    }
+  }
+  __syncthreads();
+  merge_store_rt(a, w, red_acc, red_m, red_l, NC, D);
+}
+
+// ------------------------------------------------------------------ split-K reduce
+__global__ void __launch_bounds__(128)
+splitk_reduce_kernel(const DecodeArgs a, int D) {
+  const int r = blockIdx.x;
+  const int h = blockIdx.y;
+  const int lim = __ldg(a.ctx + r);
+  const int np = (lim + a.part_tokens - 1) / a.part_tokens;
+  const int64_t obase = (int64_t)r * a.out_stride + (int64_t)h * D;
+  if (np <= 1) return;  // written (or zero-filled) by the decode kernel
+  const int npp = np < a.max_parts ? np : a.max_parts;
+  const int64_t base = ((int64_t)r * a.num_q_heads + h) * a.max_parts;
+  const float* lse = a.part_lse + base;
+  float M = -INFINITY;
+  for (int p = 0; p < npp; ++p) M = fmaxf(M, lse[p]);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+      for (int p = 0; p < npp; ++p) {
+        const float e = fast_exp2(lse[p] - M);
+        L += e;
+        O += e * a.part_out[(base + p) * D + d];
+      }
+    }
+    store_out(a, obase + d, L > 0.f ? O / L : 0.f);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static std::mutex g_mu;
+
+struct TmapEntry {
+  const void* ptr;
+  int dtype, head_dim, heads, block_size;
+  int64_t num_blocks;
+  CUtensorMap map;
+  bool used;
+};
+static TmapEntry g_tmaps[64];
+static int g_tmap_next = 0;
+
+static int get_tmap(const void* ptr, int dtype, int D, int H, int BS, int64_t nb,
+                    CUtensorMap* out) {
+  std::lock_guard<std::mutex> lock(g_mu);
+  for (auto& e : g_tmaps) {
+    if (e.used && e.ptr == ptr && e.dtype == dtype && e.head_dim == D && e.heads == H &&
+        e.block_size == BS && e.num_blocks == nb) {
+      *out = e.map;
+      return CLOVER_B200_OK;
+    }
+  }
+  if (g_encode == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    cudaError_t err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (err != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return set_error(CLOVER_B200_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  CUtensorMap m;
+  const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)(nb * BS)};
+  const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)H * D * 2};
+  const cuuint32_t box[3] = {64, 1, (cuuint32_t)BS};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUtensorMapDataType dt =
+      dtype == CLOVER_B200_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = g_encode(&m, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(CLOVER_B200_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  TmapEntry& e = g_tmaps[g_tmap_next];
+  g_tmap_next = (g_tmap_next + 1) % 64;
+  e = TmapEntry{ptr, dtype, D, H, BS, nb, m, true};
+  *out = m;
+  return CLOVER_B200_OK;
+}
+
+static bool mma_supported(int kv_dtype, int q_dtype, int D, int BS) {
+  return (kv_dtype == CLOVER_B200_BF16 || kv_dtype == CLOVER_B200_F16) &&
+         (q_dtype == CLOVER_B200_F32 || q_dtype == kv_dtype) && (D == 64 || D == 128 || D == 256) &&
+         (BS == 16 || BS == 32);
+}
+
+static int choose_partition(int max_ctx, int BS, int rows_x_kvh, bool mma) {
+  // 512-token partitions by default (flash-decoding split); shorter contexts
+  // with few (row, head) units split finer so the grid still covers the GPU.
+  int pt = 512;
+  const int min_pt = BS * kNumWarps;
+  while (pt > min_pt && (int64_t)rows_x_kvh * ((max_ctx + pt - 1) / pt) < 2 * 148) pt /= 2;
+  if (pt < min_pt) pt = min_pt;
+  pt = (pt + BS - 1) / BS * BS;
+  if (mma && pt > 32 * kNumWarps * BS) pt = 32 * kNumWarps * BS;
+  return pt;
+}
+
+template <typename Kern>
+static int set_smem(Kern k, int bytes) {
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  return check_cuda(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
+                    "cudaFuncSetAttribute");
+}
+
+template <typename T, bool QF32, int D, int BS>
+static int launch_mma(const DecodeArgs& a, const CUtensorMap& tk, const CUtensorMap& tv,
+                      dim3 grid, cudaStream_t s) {
+  using G = MmaGeom<D, BS>;
+  static uint64_t configured = 0;  // one bit per device ordinal
+  auto kern = paged_decode_mma_kernel<T, QF32, D, BS>;
+  int dev = 0;
+  int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc) return rc;
+  if (dev >= 64 || !(configured >> dev & 1)) {
+    rc = set_smem(kern, G::kSmem);
+    if (rc) return rc;
+    if (dev < 64) configured |= 1ull << dev;
+  }
+  kern<<<grid, kThreads, G::kSmem, s>>>(tk, tv, a);
+  return check_cuda(cudaGetLastError(), "paged_decode_mma launch");
+}
+
+template <typename T, bool QF32, int D>
+static int dispatch_bs(int BS, const DecodeArgs& a, const CUtensorMap& tk, const CUtensorMap& tv,
+                       dim3 grid, cudaStream_t s) {
+  return BS == 16 ? launch_mma<T, QF32, D, 16>(a, tk, tv, grid, s)
+                  : launch_mma<T, QF32, D, 32>(a, tk, tv, grid, s);
+}
+
+template <typename T, bool QF32>
+static int dispatch_d(int D, int BS, const DecodeArgs& a, const CUtensorMap& tk,
+                      const CUtensorMap& tv, dim3 grid, cudaStream_t s) {
+  switch (D) {
+    case 64: return dispatch_bs<T, QF32, 64>(BS, a, tk, tv, grid, s);
+    case 128: return dispatch_bs<T, QF32, 128>(BS, a, tk, tv, grid, s);
+    default: return dispatch_bs<T, QF32, 256>(BS, a, tk, tv, grid, s);
+  }
+}
+
+template <typename KT, int EPL>
+static int launch_simt_nc(int nc, int D, const DecodeArgs& a, dim3 grid, cudaStream_t s) {
+  switch (nc) {
+    case 1: paged_decode_simt_kernel<KT, EPL, 1><<<grid, kThreads, 0, s>>>(a, D); break;
+    case 2: paged_decode_simt_kernel<KT, EPL, 2><<<grid, kThreads, 0, s>>>(a, D); break;
+    case 4: paged_decode_simt_kernel<KT, EPL, 4><<<grid, kThreads, 0, s>>>(a, D); break;
+    default: paged_decode_simt_kernel<KT, EPL, 8><<<grid, kThreads, 0, s>>>(a, D); break;
+  }
+  return check_cuda(cudaGetLastError(), "paged_decode_simt launch");
+}
+
+template <typename KT>
+static int launch_simt(int D, int nc, const DecodeArgs& a, dim3 grid, cudaStream_t s) {
+  if (D <= 32) return launch_simt_nc<KT, 1>(nc, D, a, grid, s);
+  if (D <= 64) return launch_simt_nc<KT, 2>(nc, D, a, grid, s);
+  if (D <= 128) return launch_simt_nc<KT, 4>(nc, D, a, grid, s);
+  return launch_simt_nc<KT, 8>(nc, D, a, grid, s);
+}
+
+static int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
+
+static int64_t workspace_bytes(int64_t rows, int64_t hq, int64_t D, int64_t parts) {
+  if (parts <= 1) return 0;
+  return align256(rows * hq * parts * D * 4) + align256(rows * hq * parts * 4);
+}
+
+struct DecodePlan {
+  bool mma;
+  int cols_per_cta, col_chunks, part_tokens, max_parts;
+  int64_t workspace_bytes;
+};
+
+// The launch shape of one paged_decode call; shared by the workspace query so
+// callers size the workspace for exactly what the launch will use.
+static int make_plan(int n_seqs, int n_rows, int max_q, int max_ctx, int hq, int hkv, int D,
+                     int BS, int kv_dtype, int q_dtype, int partition_tokens, DecodePlan* pl) {
+  if (n_seqs < 0 || n_rows < 0 || hq <= 0 || hkv <= 0 || D <= 0 || BS <= 0 || max_ctx < 0 ||
+      max_q < 0)
+    return set_error(CLOVER_B200_ERR_INVALID_ARG, "paged_decode: bad sizes");
+  if (hq % hkv != 0)
+    return set_error(CLOVER_B200_ERR_INVALID_ARG, "paged_decode: num_q_heads %% num_kv_heads != 0");
+  if (q_dtype != CLOVER_B200_F32 && q_dtype != CLOVER_B200_F16 && q_dtype != CLOVER_B200_BF16)
+    return set_error(CLOVER_B200_ERR_UNSUPPORTED, "paged_decode: q dtype %d", q_dtype);
+  if (kv_dtype != CLOVER_B200_F32 && kv_dtype != CLOVER_B200_F16 && kv_dtype != CLOVER_B200_BF16)
+    return set_error(CLOVER_B200_ERR_UNSUPPORTED, "paged_decode: kv dtype %d", kv_dtype);
+  if (max_q == 0) max_q = 1;
+  const int group = hq / hkv;
+  pl->mma = mma_supported(kv_dtype, q_dtype, D, BS);
+  if (!pl->mma && D > 256)
+    return set_error(CLOVER_B200_ERR_UNSUPPORTED, "paged_decode: head_dim %d > 256", D);
+  const int ncols_seq = max_q * group;
+  if (pl->mma) {
+    pl->cols_per_cta = kMmaCols;
+  } else {
+    pl->cols_per_cta = ncols_seq >= 8 ? 8 : ncols_seq >= 4 ? 4 : ncols_seq >= 2 ? 2 : 1;
+  }
+  pl->col_chunks = (ncols_seq + pl->cols_per_cta - 1) / pl->cols_per_cta;
+  int pt = partition_tokens;
+  if (pt <= 0) {
+    pt = choose_partition(max_ctx, BS, n_seqs * hkv * pl->col_chunks, pl->mma);
+  } else {
+    if (pt % BS != 0)
+      return set_error(CLOVER_B200_ERR_INVALID_ARG, "paged_decode: partition_tokens %% block_size != 0");
+    if (pl->mma && pt > 32 * kNumWarps * BS)
+      return set_error(CLOVER_B200_ERR_INVALID_ARG, "paged_decode: partition_tokens > %d",
+                       32 * kNumWarps * BS);
+  }
+  pl->part_tokens = pt;
+  pl->max_parts = max_ctx > 0 ? (max_ctx + pt - 1) / pt : 1;
+  pl->workspace_bytes = workspace_bytes(n_rows, hq, D, pl->max_parts);
+  return CLOVER_B200_OK;
+}
+
+}  // namespace clover
+
+using namespace clover;
+
+extern "C" int64_t clover_b200_decode_workspace_bytes(
+    int32_t n_seqs, int32_t n_query_rows, int32_t max_queries_per_seq, int32_t max_ctx_len,
+    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+    int32_t kv_dtype, int32_t q_dtype, int32_t partition_tokens) {
+  DecodePlan pl;
+  if (make_plan(n_seqs, n_query_rows, max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads,
+                head_dim, block_size, kv_dtype, q_dtype, partition_tokens, &pl) != CLOVER_B200_OK)
+    return -1;
+  return pl.workspace_bytes;
+}
+
+extern "C" int clover_b200_paged_decode(
+    void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride, int32_t q_dtype,
+    const void* k_cache, const void* v_cache, int32_t kv_dtype, int64_t num_blocks,
+    int32_t block_size, const int32_t* block_tables, int32_t table_stride,
+    const int32_t* seq_rows, const int32_t* query_start_loc, const int32_t* ctx_lens,
+    int32_t n_seqs, int32_t n_query_rows, int32_t max_queries_per_seq, int32_t max_ctx_len,
+    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, float score_scale,
+    int32_t partition_tokens, void* workspace, int64_t workspace_bytes_, int32_t* dev_status,
+    void* stream) {
+  if (table_stride <= 0 || num_blocks <= 0)
+    return set_error(CLOVER_B200_ERR_INVALID_ARG, "paged_decode: bad sizes");
+  DecodePlan pl;
+  int rc = make_plan(n_seqs, n_query_rows, max_queries_per_seq, max_ctx_len, num_q_heads,
+                     num_kv_heads, head_dim, block_size, kv_dtype, q_dtype, partition_tokens, &pl);
+  if (rc) return rc;
+  if (n_seqs == 0 || n_query_rows == 0) return CLOVER_B200_OK;
+  if (!out || !q || !k_cache || !v_cache || !block_tables || !query_start_loc || !ctx_lens)
+    return set_error(CLOVER_B200_ERR_INVALID_ARG, "paged_decode: null pointer");
+  if (q_row_stride < (int64_t)num_q_heads * head_dim || out_row_stride < (int64_t)num_q_heads * head_dim)
+    return set_error(CLOVER_B200_ERR_INVALID_ARG, "paged_decode: row stride < heads*head_dim");
+  if (n_seqs > 65535 || (int64_t)num_kv_heads * pl.col_chunks > 65535)
+    return set_error(CLOVER_B200_ERR_UNSUPPORTED, "paged_decode: grid too large");
+  if (pl.mma) {
+    if ((reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 15))
+      return set_error(CLOVER_B200_ERR_INVALID_ARG, "paged_decode: cache not 16-byte aligned");
+    if (num_blocks * (int64_t)block_size > INT32_MAX)
+      return set_error(CLOVER_B200_ERR_UNSUPPORTED, "paged_decode: cache exceeds 2^31 slots");
+  }
+  const int64_t need = pl.workspace_bytes;
+  if (need > 0 && (workspace == nullptr || workspace_bytes_ < need))
+    return set_error(CLOVER_B200_ERR_WORKSPACE, "paged_decode: workspace needs %lld bytes",
+                     (long long)need);
+  const int group = num_q_heads / num_kv_heads;
+  const int pt = pl.part_tokens;
+  const int max_parts = pl.max_parts;
+  const int cols_per_cta = pl.cols_per_cta;
+  const int col_chunks = pl.col_chunks;
+  const bool mma = pl.mma;
+
+  DecodeArgs a;
+  a.out = out;
+  a.out_stride = out_row_stride;
+  a.q = q;
+  a.q_stride = q_row_stride;
+  a.q_dtype = q_dtype;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.tables = block_tables;
+  a.table_stride = table_stride;
+  a.seq_rows = seq_rows;
+  a.qsl = query_start_loc;
+  a.ctx = ctx_lens;
+  a.num_q_heads = num_q_heads;
+  a.num_kv_heads = num_kv_heads;
+  a.group = group;
+  a.block_size = block_size;
+  a.num_blocks = num_blocks;
+  a.scale_log2 = score_scale * 1.4426950408889634f;
+  a.part_tokens = pt;
+  a.max_parts = max_parts;
+  a.cols_per_cta = cols_per_cta;
+  a.col_chunks = col_chunks;
+  a.part_out = need > 0 ? static_cast<float*>(workspace) : nullptr;
+  a.part_lse = need > 0 ? reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                                   align256((int64_t)n_query_rows * num_q_heads *
+                                                            max_parts * head_dim * 4))
+                        : nullptr;
+  a.status = dev_status;
+
+  cudaStream_t s = (cudaStream_t)stream;
+  const dim3 grid(max_parts, num_kv_heads * col_chunks, n_seqs);
+  if (mma) {
+    CUtensorMap tk, tv;
+    rc = get_tmap(k_cache, kv_dtype, head_dim, num_kv_heads, block_size, num_blocks, &tk);
+    if (rc) return rc;
+    rc = get_tmap(v_cache, kv_dtype, head_dim, num_kv_heads, block_size, num_blocks, &tv);
+    if (rc) return rc;
+    if (kv_dtype == CLOVER_B200_BF16) {
+      rc = q_dtype == CLOVER_B200_F32
+               ? dispatch_d<__nv_bfloat16, true>(head_dim, block_size, a, tk, tv, grid, s)
+               : dispatch_d<__nv_bfloat16, false>(head_dim, block_size, a, tk, tv, grid, s);
+    } else {
+      rc = q_dtype == CLOVER_B200_F32
+               ? dispatch_d<__half, true>(head_dim, block_size, a, tk, tv, grid, s)
+               : dispatch_d<__half, false>(head_dim, block_size, a, tk, tv, grid, s);
+    }
+  } else {
+    switch (kv_dtype) {
+      case CLOVER_B200_F32: rc = launch_simt<float>(head_dim, cols_per_cta, a, grid, s); break;
+      case CLOVER_B200_F16: rc = launch_simt<__half>(head_dim, cols_per_cta, a, grid, s); break;
+      default: rc = launch_simt<__nv_bfloat16>(head_dim, cols_per_cta, a, grid, s); break;
+    }
+  }
+  if (rc) return rc;
+  if (max_parts > 1) {
+    // Rows with several partitions are combined here; single-partition rows
+    // were written by the decode kernel and return at once.
+    splitk_reduce_kernel<<<dim3(n_query_rows, num_q_heads), 128, 0, s>>>(a, head_dim);
+    rc = check_cuda(cudaGetLastError(), "splitk_reduce launch");
+  }
+  return rc;
+}

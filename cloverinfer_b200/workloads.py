@@ -1,0 +1,98 @@
+"""Seeded synthetic workloads for the five reference configurations.
+
+Shapes and value distributions follow the configurations the upstream metric
+is quoted on (no dataset is involved; synthetic inputs stand in):
+
+  c1  OPT-125m shape, CPU-reference case: 12 layers, 12 heads (MHA), D=64, fp32,
+      batch 4, contexts U[128, 512], block 16, tables from a 256-block pool.
+  c2  Qwen2.5-7B GQA: 28 q / 4 KV heads, D=128, bf16, block 16, batch 32,
+      contexts U[1024, 4096], values N(0,1)*0.5, random non-contiguous tables.
+  c3  Llama-3-8B long context: 32 q / 8 KV heads, D=128, bf16, block 16,
+      batch 8, every context 32768, split-K with 512-token partitions.
+  c4  mixed continuous batching, Llama-3-8B shape, fp16, batch 256, contexts
+      log-uniform [16, 16384], 1-4 new tokens per sequence, block 32,
+      2M-block pool (head-sharded over 8 GPUs), 30 % of blocks churned per step.
+  c5  Llama-3-70B shape: 64 q / 8 KV heads, D=128, bf16, block 16, batch 64,
+      contexts U[8192, 65536], one KV head per GPU on 8 GPUs.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import List
+
+import torch
+
+
+@dataclass
+class Config:
+    name: str
+    num_layers: int
+    num_q_heads: int
+    num_kv_heads: int
+    head_dim: int
+    dtype: torch.dtype
+    block_size: int
+    batch: int
+    ctx_lo: int
+    ctx_hi: int
+    ctx_dist: str = "uniform"      # uniform | loguniform | fixed
+    new_lo: int = 1
+    new_hi: int = 1
+    pool_blocks: int = 0           # 0: just enough (+ slack)
+    value_scale: float = 1.0
+    partition_tokens: int = 0
+    churn: float = 0.0
+    score_scale: float = field(default=0.0)
+
+    def __post_init__(self):
+        if not self.score_scale:
+            self.score_scale = 1.0 / math.sqrt(self.head_dim)
+
+    @property
+    def group(self) -> int:
+        return self.num_q_heads // self.num_kv_heads
+
+
+CONFIGS = {
+    "c1": Config("c1-opt125m-fp32", 12, 12, 12, 64, torch.float32, 16, 4, 128, 512,
+                 pool_blocks=256, score_scale=1.0 / 8.0),
+    "c2": Config("c2-qwen2.5-7b-gqa-bf16", 1, 28, 4, 128, torch.bfloat16, 16, 32, 1024, 4096,
+                 value_scale=0.5),
+    "c3": Config("c3-llama3-8b-32k-bf16", 1, 32, 8, 128, torch.bfloat16, 16, 8, 32768, 32768,
+                 ctx_dist="fixed", partition_tokens=512),
+    "c4": Config("c4-mixed-cb-llama3-8b-fp16", 1, 32, 8, 128, torch.float16, 32, 256, 16, 16384,
+                 ctx_dist="loguniform", new_lo=1, new_hi=4, pool_blocks=2 * 1024 * 1024, churn=0.3),
+    "c5": Config("c5-llama3-70b-bf16", 1, 64, 8, 128, torch.bfloat16, 16, 64, 8192, 65536),
+}
+
+
+def context_lengths(cfg: Config, seed: int, batch: int = 0) -> List[int]:
+    g = torch.Generator().manual_seed(seed)
+    b = batch or cfg.batch
+    if cfg.ctx_dist == "fixed":
+        return [cfg.ctx_hi] * b
+    if cfg.ctx_dist == "loguniform":
+        u = torch.rand(b, generator=g, dtype=torch.float64)
+        lo, hi = math.log(cfg.ctx_lo), math.log(cfg.ctx_hi)
+        return [int(round(math.exp(lo + (hi - lo) * float(x)))) for x in u]
+    return torch.randint(cfg.ctx_lo, cfg.ctx_hi + 1, (b,), generator=g).tolist()
+
+
+def new_tokens(cfg: Config, seed: int, batch: int = 0) -> List[int]:
+    g = torch.Generator().manual_seed(seed + 1)
+    b = batch or cfg.batch
+    return torch.randint(cfg.new_lo, cfg.new_hi + 1, (b,), generator=g).tolist()
+
+
+def randn(shape, seed: int, scale: float, dtype: torch.dtype, device="cpu") -> torch.Tensor:
+    """N(0,1)*scale rounded to ``dtype`` (generated in fp32 from a seed)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    return (torch.randn(shape, generator=g, device=device, dtype=torch.float32) * scale).to(dtype)
+
+
+def kv_bytes(ctx_per_seq: List[int], num_kv_heads: int, head_dim: int, dtype: torch.dtype) -> int:
+    """Algorithmic KV bytes one decode step reads: sum_s ctx_s * Hkv * D * 2 * e."""
+    e = torch.empty((), dtype=dtype).element_size()
+    return sum(ctx_per_seq) * num_kv_heads * head_dim * 2 * e

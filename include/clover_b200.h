@@ -1,0 +1,186 @@
+/*
+ * clover_b200.h — C ABI of the B200-native paged decode-attention library
+ * (libclover_b200.so).
+ *
+ * It is the drop-in boundary for CloverInfer's attention hot path: the
+ * per-layer decode of `AttentionNode` (src/core/nodes.py:154) through
+ * `CpuAttentionBackend.decode_layer` (src/core/attention_backend.py:82-123)
+ * and the paged GPU op behind `KVCacheManager` (src/core/memory_manager.py:19-239,
+ * src/kernels/csrc/manager.cpp:19-42).
+ *
+ * Conventions
+ *   - Plain device pointers and sizes; no framework types.  All memory is
+ *     caller-owned (the caller allocates caches, tables, outputs and the
+ *     split-K workspace).  Nothing in this header allocates device memory.
+ *   - Every entry point returns CLOVER_B200_OK (0) or a negative
+ *     CLOVER_B200_ERR_* code and never throws; clover_b200_last_error()
+ *     returns a thread-local description of the last failure.
+ *   - Work is enqueued on `stream` (a cudaStream_t passed as void*; NULL =
+ *     the legacy default stream) and is asynchronous.
+ *   - Kernels report bad indices (slot or block id out of range, table
+ *     overflow, allocator exhaustion) by OR-ing CLOVER_B200_DEV_* bits into
+ *     the caller's int32 `dev_status` word; the offending element is skipped.
+ *     No kernel traps.
+ *   - Layouts follow KVCacheManager: one cache per layer for K and one for V,
+ *     `[num_blocks, block_size, num_kv_heads, head_dim]` contiguous
+ *     (memory_manager.py:35-46); token `t` of a sequence lives in slot
+ *     `table[t / block_size] * block_size + t % block_size`; padded tables
+ *     hold -1 (memory_manager.py:167).
+ */
+#ifndef CLOVER_B200_H
+#define CLOVER_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CLOVER_B200_API __attribute__((visibility("default")))
+#else
+#define CLOVER_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (host return values) ---------------------------------- */
+#define CLOVER_B200_OK               0
+#define CLOVER_B200_ERR_INVALID_ARG -1  /* null pointer, bad size or stride   */
+#define CLOVER_B200_ERR_UNSUPPORTED -2  /* dtype / head_dim / block_size combo */
+#define CLOVER_B200_ERR_CUDA        -3  /* a CUDA runtime/driver call failed   */
+#define CLOVER_B200_ERR_WORKSPACE   -4  /* split-K workspace too small         */
+
+/* ---- device status bits (OR-ed into *dev_status by kernels) -------------- */
+#define CLOVER_B200_DEV_BAD_SLOT      0x1  /* slot >= num_blocks*block_size        */
+#define CLOVER_B200_DEV_BAD_BLOCK     0x2  /* table entry outside [0, num_blocks)  */
+#define CLOVER_B200_DEV_TABLE_FULL    0x4  /* sequence needs more than table_stride blocks */
+#define CLOVER_B200_DEV_OOM           0x8  /* free stack exhausted (batch left unchanged) */
+#define CLOVER_B200_DEV_TIMEOUT      0x10  /* a bounded wait gave up                */
+#define CLOVER_B200_DEV_CTX_RANGE    0x20  /* a context exceeds max_ctx_len        */
+
+/* ---- dtypes --------------------------------------------------------------- */
+#define CLOVER_B200_F32  0
+#define CLOVER_B200_F16  1
+#define CLOVER_B200_BF16 2
+
+/* Library version (major*10000 + minor*100 + patch). */
+CLOVER_B200_API int clover_b200_version(void);
+
+/* Thread-local description of the last error returned on this thread. */
+CLOVER_B200_API const char* clover_b200_last_error(void);
+
+/*
+ * Block allocator — the free-block stack and block tables of
+ * KVCacheManager, resident in device memory.
+ *
+ * free_stack[num_blocks] int32 and *free_top (int32, device) form the LIFO
+ * stack of memory_manager.py:49 (`list(range(num_blocks))`, top = length):
+ * a pop takes free_stack[top-1].  block_tables is [rows, table_stride] int32
+ * (-1 padded) and table_len[rows] the number of blocks each row owns.
+ */
+
+/*
+ * Grow rows so that row rows[i] can hold target_tokens[i] tokens, popping the
+ * missing blocks in item order and, within an item, in table order — the
+ * same blocks the upstream manager hands out for the equivalent sequence of
+ * `allocate(id, seq_len)` (target = seq_len + 1, memory_manager.py:55-72) and
+ * `append_slot(id)` calls (target = len + 1, :95-121).  If the whole batch
+ * does not fit, nothing changes and CLOVER_B200_DEV_OOM is raised.
+ * Replaces: KVCacheManager.allocate / append_slot block growth (memory_manager.py:55-72, :95-121).
+ */
+CLOVER_B200_API int clover_b200_block_reserve(int32_t* free_stack, int32_t* free_top, int32_t num_blocks,
+                              int32_t* block_tables, int32_t table_stride, int32_t* table_len,
+                              const int32_t* rows, const int32_t* target_tokens, int32_t n_items,
+                              int32_t block_size, int32_t* dev_status, void* stream);
+
+/*
+ * Return every block of rows[0..n_items) to the stack, row by row in table
+ * order (the upstream `free`, memory_manager.py:134-143), reset the rows to
+ * -1 and their length to 0.  Rows that own no block are a no-op.
+ * Replaces: KVCacheManager.free (memory_manager.py:134-143).
+ */
+CLOVER_B200_API int clover_b200_block_free(int32_t* free_stack, int32_t* free_top, int32_t num_blocks,
+                           int32_t* block_tables, int32_t table_stride, int32_t* table_len,
+                           const int32_t* rows, int32_t n_items, int32_t* dev_status, void* stream);
+
+/*
+ * Slot mapping for new tokens: item i writes tokens at positions
+ * positions[i] .. positions[i] + (token_offsets[i+1]-token_offsets[i]) - 1
+ * of table row rows[i]; slot_mapping[token_offsets[i] + j] receives the flat
+ * slot of position positions[i]+j.  The `(block, offset)` pair that
+ * append_slot returns is (slot / block_size, slot % block_size).
+ * Replaces: KVCacheManager.append_slot's slot arithmetic (memory_manager.py:113-121).
+ */
+CLOVER_B200_API int clover_b200_compute_slots(const int32_t* block_tables, int32_t table_stride,
+                              const int32_t* rows, const int32_t* positions,
+                              const int32_t* token_offsets, int32_t n_items, int32_t block_size,
+                              int64_t num_blocks, int64_t* slot_mapping, int32_t* dev_status,
+                              void* stream);
+
+/*
+ * KV append (reshape-and-cache): copy k_new/v_new token j ([num_kv_heads,
+ * head_dim], token stride `new_token_stride` elements) into slot
+ * slot_mapping[j] of k_cache/v_cache.  Negative slots are skipped (padding);
+ * slots >= num_blocks*block_size raise CLOVER_B200_DEV_BAD_SLOT.  A bit copy.
+ * Replaces: KVCacheManager.write_new_kv / load_initial_kv slice stores
+ * (memory_manager.py:74-93, :123-132) and the torch.cat append of
+ * CpuAttentionBackend.decode_layer (attention_backend.py:105-110).
+ */
+CLOVER_B200_API int clover_b200_kv_append(void* k_cache, void* v_cache, const void* k_new, const void* v_new,
+                          int64_t new_token_stride, const int64_t* slot_mapping, int64_t n_tokens,
+                          int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                          int64_t num_blocks, int32_t dtype, int32_t* dev_status, void* stream);
+
+/*
+ * Bytes of split-K workspace clover_b200_paged_decode needs for a call with
+ * the same sizes, dtypes and partition_tokens (0 = the library's choice);
+ * 0 when every context fits one partition, -1 on invalid sizes.
+ */
+CLOVER_B200_API int64_t clover_b200_decode_workspace_bytes(int32_t n_seqs, int32_t n_query_rows,
+                                           int32_t max_queries_per_seq, int32_t max_ctx_len,
+                                           int32_t num_q_heads, int32_t num_kv_heads,
+                                           int32_t head_dim, int32_t block_size, int32_t kv_dtype,
+                                           int32_t q_dtype, int32_t partition_tokens);
+
+/*
+ * Paged decode attention with GQA and split-K (flash-decoding).
+ *
+ * Batch of n_seqs sequences; sequence b owns query rows
+ * query_start_loc[b] .. query_start_loc[b+1]-1 (one row per new token; a
+ * plain decode step has query_start_loc = 0,1,..,n_seqs) and block-table row
+ * seq_rows ? seq_rows[b] : b.  Query row r attends causally to tokens
+ * [0, ctx_lens[r]) of its sequence.
+ *
+ *   q   [n_rows, num_q_heads, head_dim]  row stride q_row_stride elements,
+ *                                          dtype q_dtype (F32 or kv_dtype)
+ *   out [n_rows, num_q_heads, head_dim]  row stride out_row_stride, dtype q_dtype
+ *   out[r,h,:] = softmax(score_scale * q[r,h,:] . K^T) . V  over the KV head
+ *                h / (num_q_heads / num_kv_heads), accumulated in fp32.
+ *
+ * score_scale is applied by the kernel (q may be pre-scaled, as OPT does
+ * upstream: model_adapter.py:373, :386).  partition_tokens = 0 lets the
+ * library pick the split; workspace must hold
+ * clover_b200_decode_workspace_bytes(...) bytes (device) — it may be NULL
+ * when every context fits in one partition.  Within a call, zero-length
+ * contexts produce zeros.
+ * Replaces: CpuAttentionBackend.decode_layer scoring (attention_backend.py:113-118),
+ * KVCacheManager.attention (memory_manager.py:175-190) and
+ * paged_attention (src/kernels/csrc/manager.cpp:19-38, attention.cu:16-149).
+ */
+CLOVER_B200_API int clover_b200_paged_decode(void* out, int64_t out_row_stride,
+                             const void* q, int64_t q_row_stride, int32_t q_dtype,
+                             const void* k_cache, const void* v_cache, int32_t kv_dtype,
+                             int64_t num_blocks, int32_t block_size,
+                             const int32_t* block_tables, int32_t table_stride,
+                             const int32_t* seq_rows, const int32_t* query_start_loc,
+                             const int32_t* ctx_lens, int32_t n_seqs, int32_t n_query_rows,
+                             int32_t max_queries_per_seq, int32_t max_ctx_len,
+                             int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                             float score_scale, int32_t partition_tokens,
+                             void* workspace, int64_t workspace_bytes,
+                             int32_t* dev_status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CLOVER_B200_H */

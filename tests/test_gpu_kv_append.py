@@ -1,0 +1,88 @@
+"""KV append (reshape-and-cache) and slot mapping: bit-exact on the GPU."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import gpu
+
+pytestmark = gpu
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("heads,dim,bs", [(8, 128, 16), (1, 128, 16), (12, 64, 16), (2, 32, 32), (3, 40, 8)])
+def test_append_bit_exact(dtype, heads, dim, bs):
+    from cloverinfer_b200 import _lib
+    nb = 97
+    dev = "cuda"
+    g = torch.Generator().manual_seed(heads * 1000 + dim)
+    kc = torch.randn(nb, bs, heads, dim, generator=g).to(dtype).to(dev)
+    vc = torch.randn(nb, bs, heads, dim, generator=g).to(dtype).to(dev)
+    n = 300
+    slots = torch.randperm(nb * bs, generator=g)[:n].to(torch.int64)
+    slots[::17] = -1  # padding tokens are skipped
+    kn = torch.randn(n, heads, dim, generator=g).to(dtype)
+    vn = torch.randn(n, heads, dim, generator=g).to(dtype)
+    ref_k = kc.cpu().reshape(nb * bs, heads, dim).clone()
+    ref_v = vc.cpu().reshape(nb * bs, heads, dim).clone()
+    keep = slots >= 0
+    ref_k[slots[keep]] = kn[keep]
+    ref_v[slots[keep]] = vn[keep]
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    _lib.kv_append(kc, vc, kn.to(dev), vn.to(dev), slots.to(dev), status)
+    assert int(status.item()) == 0
+    assert torch.equal(kc.cpu().reshape(nb * bs, heads, dim), ref_k)
+    assert torch.equal(vc.cpu().reshape(nb * bs, heads, dim), ref_v)
+
+
+def test_append_strided_source_and_bad_slot():
+    from cloverinfer_b200 import _lib
+    dev = "cuda"
+    nb, bs, h, d = 8, 16, 2, 64
+    kc = torch.zeros(nb, bs, h, d, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    # rows of a fused [n, 3, H, D] qkv-like buffer: token stride 3*H*D
+    fused = torch.randn(5, 3, h, d, device=dev).to(torch.bfloat16)
+    kn, vn = fused[:, 1], fused[:, 2]
+    slots = torch.tensor([0, 17, nb * bs - 1, nb * bs, -1], dtype=torch.int64, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    _lib.kv_append(kc, vc, kn, vn, slots, status)
+    assert int(status.item()) & _lib.DEV_BAD_SLOT
+    flat_k = kc.reshape(-1, h, d)
+    assert torch.equal(flat_k[0], kn[0]) and torch.equal(flat_k[17], kn[1])
+    assert torch.equal(flat_k[nb * bs - 1], kn[2])
+    assert torch.equal(vc.reshape(-1, h, d)[17], vn[1])
+    assert int((flat_k != 0).any(dim=(1, 2)).sum()) == 3
+
+
+def test_compute_slots_matches_upstream_arithmetic():
+    """slot = table[pos // bs] * bs + pos % bs (memory_manager.py:113-121)."""
+    from cloverinfer_b200 import PagedKVPool
+    from oracle import KVCacheOracle
+    pool = PagedKVPool(200, 16, 1, 64, device="cuda", max_seqs=16, max_blocks_per_seq=32)
+    pool.shuffle_free_stack(9)
+    ref = KVCacheOracle(200, 16, 1, 64, with_storage=False)
+    ref.free_blocks = pool.free_stack.cpu().tolist()
+    lens = [5, 16, 17, 100, 255, 0, 31]
+    rows = list(range(len(lens)))
+    for r, n in zip(rows, lens):
+        ref.allocate(f"s{r}", n)
+    pool.reserve(rows, [n + 1 for n in lens])
+    n_new = [1, 3, 2, 4, 1, 2, 1]
+    for r, (n, k) in enumerate(zip(lens, n_new)):
+        for _ in range(k):
+            ref.append_slot(f"s{r}")
+    pool.reserve(rows, [n + k for n, k in zip(lens, n_new)])
+    offs = [0]
+    for k in n_new:
+        offs.append(offs[-1] + k)
+    dev = pool.device
+    slots = pool.slots(torch.tensor(rows, dtype=torch.int32, device=dev),
+                       torch.tensor(lens, dtype=torch.int32, device=dev),
+                       torch.tensor(offs, dtype=torch.int32, device=dev), offs[-1]).cpu().tolist()
+    want = []
+    for r, (n, k) in enumerate(zip(lens, n_new)):
+        want += [ref.slot(f"s{r}", n + j) for j in range(k)]
+    assert slots == want
+    pool.check_status()
