@@ -332,6 +332,7 @@ def run_b200(args):
     dec_ms = d0.elapsed_time(d1) / args.steps
     clk = clocks.stop()
     st["pool"].check_status()
+    used_graph = graph is not None
     del graph, dec_graph
 
     # ---------------- e2e through the public API (host buffers in, host out)
@@ -350,7 +351,7 @@ def run_b200(args):
                    "num_q_heads": cfg.num_q_heads, "num_kv_heads": cfg.num_kv_heads,
                    "head_dim": cfg.head_dim, "block_size": cfg.block_size,
                    "partition_tokens": cfg.partition_tokens,
-                   "parallelism": f"kv-head-shard{world}", "cuda_graph": graph is not None or not args.no_graph,
+                   "parallelism": f"kv-head-shard{world}", "cuda_graph": used_graph,
                    "l2": "inputs > L2 (KV %.0f MB per GPU)" % (local_kv / 1e6)},
         "steps_per_s": round(1e3 / ms, 2),
         "tokens_per_s": round(B * 1e3 / ms, 2),
