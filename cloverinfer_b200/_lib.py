@@ -49,7 +49,11 @@ SIGNATURES = {
     "clover_b200_paged_decode": (ctypes.c_int, [
         _P, _I64, _P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _I32, _P, _P, _P,
         _I32, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _P, _P]),
+    "clover_b200_paged_decode_noalloc": (ctypes.c_int, [
+        _P, _I64, _P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _I32, _P, _P, _P,
+        _I32, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _P]),
 }
+NOALLOC_SCRATCH_BYTES = 16 << 20  # CLOVER_B200_NOALLOC_SCRATCH_BYTES
 
 
 class CloverB200Error(RuntimeError):

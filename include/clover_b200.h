@@ -179,6 +179,31 @@ CLOVER_B200_API int clover_b200_paged_decode(void* out, int64_t out_row_stride,
                              void* workspace, int64_t workspace_bytes,
                              int32_t* dev_status, void* stream);
 
+/*
+ * Allocation-free paged decode.  No counterpart in the upstream project: it
+ * exists for callers that cannot call cudaMalloc (a serving engine that owns
+ * all of HBM through its own pool, or a foreign-function host without a CUDA
+ * allocator).  Same arguments and results as clover_b200_paged_decode minus
+ * the workspace: split-K scratch comes from a static device array of
+ * CLOVER_B200_NOALLOC_SCRATCH_BYTES held by every GPU that loads the library.
+ * Calls needing more scratch than that return CLOVER_B200_ERR_WORKSPACE.  The
+ * first call on a device looks the array up (make it before any stream
+ * capture).  All calls share the array: calls that overlap on the GPU race.
+ */
+#define CLOVER_B200_NOALLOC_SCRATCH_BYTES (16ll << 20)
+
+CLOVER_B200_API int clover_b200_paged_decode_noalloc(void* out, int64_t out_row_stride,
+                             const void* q, int64_t q_row_stride, int32_t q_dtype,
+                             const void* k_cache, const void* v_cache, int32_t kv_dtype,
+                             int64_t num_blocks, int32_t block_size,
+                             const int32_t* block_tables, int32_t table_stride,
+                             const int32_t* seq_rows, const int32_t* query_start_loc,
+                             const int32_t* ctx_lens, int32_t n_seqs, int32_t n_query_rows,
+                             int32_t max_queries_per_seq, int32_t max_ctx_len,
+                             int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                             float score_scale, int32_t partition_tokens,
+                             int32_t* dev_status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
