@@ -21,6 +21,16 @@ __device__ __forceinline__ int32_t blocks_for(int32_t tokens, int32_t bs) {
   return tokens <= 0 ? 0 : (tokens + bs - 1) / bs;
 }
 
+// Index of the item whose [off[i], off[i] + n[i]) range holds k (off ascending).
+__device__ __forceinline__ int find_item(const int32_t* off, int n, int32_t k) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (off[mid] <= k) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
 __global__ void __launch_bounds__(kAllocThreads)
 block_reserve_kernel(int32_t* __restrict__ free_stack, int32_t* __restrict__ free_top,
                      int32_t num_blocks, int32_t* __restrict__ tables, int32_t stride,
@@ -33,7 +43,8 @@ block_reserve_kernel(int32_t* __restrict__ free_stack, int32_t* __restrict__ fre
     typename Scan::TempStorage scan;
     typename Reduce::TempStorage reduce;
   } tmp;
-  __shared__ int32_t s_total, s_bad;
+  __shared__ int32_t s_off[kAllocThreads], s_row[kAllocThreads], s_have[kAllocThreads];
+  __shared__ int32_t s_total, s_bad, s_chunk;
   const int tid = threadIdx.x;
   if (tid == 0) {
     s_total = 0;
@@ -41,7 +52,7 @@ block_reserve_kernel(int32_t* __restrict__ free_stack, int32_t* __restrict__ fre
   }
   __syncthreads();
 
-  // Pass 1: total demand and validity.
+  // Pass 1: total demand and validity (the batch is all-or-nothing).
   for (int base = 0; base < n; base += kAllocThreads) {
     const int i = base + tid;
     int32_t need = 0, bad = 0;
@@ -66,10 +77,12 @@ block_reserve_kernel(int32_t* __restrict__ free_stack, int32_t* __restrict__ fre
     return;
   }
 
-  // Pass 2: pop in item order (item i takes stack[top-1-off_i-j], j = 0..need_i-1).
+  // Pass 2: pops in item order — item i takes stack[top-1-(off_i+j)], j < need_i.
+  // The pops of a chunk are spread over all threads (binary search of the scan).
   int32_t running = 0;
   for (int base = 0; base < n; base += kAllocThreads) {
     const int i = base + tid;
+    const int cnt = min(kAllocThreads, n - base);
     int32_t need = 0, have = 0, row = 0;
     if (i < n) {
       row = rows[i];
@@ -79,11 +92,18 @@ block_reserve_kernel(int32_t* __restrict__ free_stack, int32_t* __restrict__ fre
     }
     int32_t off, chunk_total;
     Scan(tmp.scan).ExclusiveSum(need, off, chunk_total);
-    for (int32_t j = 0; j < need; ++j) {
-      tables[(int64_t)row * stride + have + j] = free_stack[top - 1 - (running + off + j)];
+    s_off[tid] = off;
+    s_row[tid] = row;
+    s_have[tid] = have;
+    if (tid == 0) s_chunk = chunk_total;
+    __syncthreads();
+    for (int32_t k = tid; k < s_chunk; k += kAllocThreads) {
+      const int it = find_item(s_off, cnt, k);
+      const int32_t j = k - s_off[it];
+      tables[(int64_t)s_row[it] * stride + s_have[it] + j] = free_stack[top - 1 - (running + k)];
     }
     if (i < n && need > 0) table_len[row] = have + need;
-    running += chunk_total;
+    running += s_chunk;
     __syncthreads();
   }
   if (tid == 0) *free_top = top - s_total;
@@ -100,7 +120,8 @@ block_free_kernel(int32_t* __restrict__ free_stack, int32_t* __restrict__ free_t
     typename Scan::TempStorage scan;
     typename Reduce::TempStorage reduce;
   } tmp;
-  __shared__ int32_t s_total;
+  __shared__ int32_t s_off[kAllocThreads], s_row[kAllocThreads];
+  __shared__ int32_t s_total, s_chunk;
   const int tid = threadIdx.x;
   if (tid == 0) s_total = 0;
   __syncthreads();
@@ -116,9 +137,11 @@ block_free_kernel(int32_t* __restrict__ free_stack, int32_t* __restrict__ free_t
     if (tid == 0) raise_status(status, CLOVER_B200_DEV_BAD_BLOCK);
     return;
   }
+  // Pushes in item order, each row's blocks in table order.
   int32_t running = 0;
   for (int base = 0; base < n; base += kAllocThreads) {
     const int i = base + tid;
+    const int cnt = min(kAllocThreads, n - base);
     int32_t len = 0, row = 0;
     if (i < n) {
       row = rows[i];
@@ -126,30 +149,35 @@ block_free_kernel(int32_t* __restrict__ free_stack, int32_t* __restrict__ free_t
     }
     int32_t off, chunk_total;
     Scan(tmp.scan).ExclusiveSum(len, off, chunk_total);
-    for (int32_t j = 0; j < len; ++j) {
-      int32_t* e = tables + (int64_t)row * stride + j;
-      free_stack[top + running + off + j] = *e;
+    s_off[tid] = off;
+    s_row[tid] = row;
+    if (tid == 0) s_chunk = chunk_total;
+    __syncthreads();
+    for (int32_t k = tid; k < s_chunk; k += kAllocThreads) {
+      const int it = find_item(s_off, cnt, k);
+      int32_t* e = tables + (int64_t)s_row[it] * stride + (k - s_off[it]);
+      free_stack[top + running + k] = *e;
       *e = -1;
     }
+    __syncthreads();
     if (i < n) table_len[row] = 0;
-    running += chunk_total;
+    running += s_chunk;
     __syncthreads();
   }
   if (tid == 0) *free_top = top + s_total;
 }
 
-__global__ void compute_slots_kernel(const int32_t* __restrict__ tables, int32_t stride,
-                                     const int32_t* __restrict__ rows,
-                                     const int32_t* __restrict__ positions,
-                                     const int32_t* __restrict__ offsets, int32_t n, int32_t bs,
-                                     int64_t num_blocks, int64_t* __restrict__ slots,
-                                     int32_t* __restrict__ status) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
+// One CTA per item; its threads cover the item's new tokens.
+__global__ void __launch_bounds__(128)
+compute_slots_kernel(const int32_t* __restrict__ tables, int32_t stride,
+                     const int32_t* __restrict__ rows, const int32_t* __restrict__ positions,
+                     const int32_t* __restrict__ offsets, int32_t bs, int64_t num_blocks,
+                     int64_t* __restrict__ slots, int32_t* __restrict__ status) {
+  const int i = blockIdx.x;
   const int32_t* tab = tables + (int64_t)rows[i] * stride;
   const int32_t pos0 = positions[i];
   const int32_t t0 = offsets[i], t1 = offsets[i + 1];
-  for (int32_t t = t0; t < t1; ++t) {
+  for (int32_t t = t0 + threadIdx.x; t < t1; t += blockDim.x) {
     const int32_t pos = pos0 + (t - t0);
     const int32_t bi = pos / bs;
     int64_t slot = -1;
@@ -214,9 +242,8 @@ extern "C" int clover_b200_compute_slots(const int32_t* block_tables, int32_t ta
   if (n_items == 0) return CLOVER_B200_OK;
   if (!block_tables || !rows || !positions || !token_offsets || !slot_mapping)
     return set_error(CLOVER_B200_ERR_INVALID_ARG, "compute_slots: null pointer");
-  const int threads = 128;
-  compute_slots_kernel<<<(n_items + threads - 1) / threads, threads, 0, (cudaStream_t)stream>>>(
-      block_tables, table_stride, rows, positions, token_offsets, n_items, block_size,
-      num_blocks, slot_mapping, dev_status);
+  compute_slots_kernel<<<n_items, 128, 0, (cudaStream_t)stream>>>(
+      block_tables, table_stride, rows, positions, token_offsets, block_size, num_blocks,
+      slot_mapping, dev_status);
   return check_cuda(cudaGetLastError(), "compute_slots launch");
 }

@@ -38,9 +38,25 @@
 
 namespace clover {
 
-constexpr int kNumWarps = 4;
+constexpr int kNumWarps = 4;  // SIMT path
 constexpr int kThreads = kNumWarps * 32;
 constexpr int kMmaCols = 8;
+
+// Tensor-core path launch shape (compile-time knobs).
+#ifndef CLOVER_MMA_WARPS
+#define CLOVER_MMA_WARPS 2
+#endif
+#ifndef CLOVER_MMA_STAGES
+#define CLOVER_MMA_STAGES 2
+#endif
+#ifndef CLOVER_MMA_STAGE_TOKENS
+#define CLOVER_MMA_STAGE_TOKENS 16
+#endif
+#ifndef CLOVER_MMA_MIN_CTAS
+#define CLOVER_MMA_MIN_CTAS 6
+#endif
+constexpr int kMmaWarps = CLOVER_MMA_WARPS;
+constexpr int kMmaThreads = kMmaWarps * 32;
 
 struct DecodeArgs {
   void* out;
@@ -113,7 +129,7 @@ struct CtaWork {
 
 // Columns whose context is empty attend to nothing: their output is zero.
 __device__ __forceinline__ void zero_empty_columns(const DecodeArgs& a, const CtaWork& w, int D) {
-  for (int idx = threadIdx.x; idx < a.cols_per_cta * D; idx += kThreads) {
+  for (int idx = threadIdx.x; idx < a.cols_per_cta * D; idx += blockDim.x) {
     const int col = idx / D;
     const ColInfo ci = col_info(a, w.row0, w.nq, w.kvh, w.chunk * a.cols_per_cta + col);
     if (ci.valid && ci.limit <= 0)
@@ -154,11 +170,11 @@ __device__ __forceinline__ bool cta_work(const DecodeArgs& a, CtaWork& w, int D)
 
 // Merge per-warp (m, l, O) partial states held in shared memory and store
 // either the final output (single-partition rows) or the split-K partial.
-// red_acc: [kNumWarps][cols][D+4], red_m/red_l: [kNumWarps][cols].
+// red_acc: [nw][cols][D+4], red_m/red_l: [nw][cols].
 __device__ __forceinline__ void merge_store_rt(const DecodeArgs& a, const CtaWork& w,
                                                const float* red_acc, const float* red_m,
-                                               const float* red_l, int cols, int D) {
-  for (int idx = threadIdx.x; idx < cols * D; idx += kThreads) {
+                                               const float* red_l, int cols, int D, int nw) {
+  for (int idx = threadIdx.x; idx < cols * D; idx += nw * 32) {
     const int col = idx / D;
     const int dim = idx - col * D;
     const ColInfo ci = col_info(a, w.row0, w.nq, w.kvh, w.chunk * a.cols_per_cta + col);
@@ -169,11 +185,11 @@ __device__ __forceinline__ void merge_store_rt(const DecodeArgs& a, const CtaWor
     }
     float M = -INFINITY;
 #pragma unroll
-    for (int k = 0; k < kNumWarps; ++k) M = fmaxf(M, red_m[k * cols + col]);
+    for (int k = 0; k < nw; ++k) M = fmaxf(M, red_m[k * cols + col]);
     float L = 0.f, O = 0.f;
     if (M != -INFINITY) {
 #pragma unroll
-      for (int k = 0; k < kNumWarps; ++k) {
+      for (int k = 0; k < nw; ++k) {
         const float e = fast_exp2(red_m[k * cols + col] - M);
         L += red_l[k * cols + col] * e;
         O += red_acc[(k * cols + col) * (D + 4) + dim] * e;
@@ -192,35 +208,46 @@ __device__ __forceinline__ void merge_store_rt(const DecodeArgs& a, const CtaWor
 }
 
 // ------------------------------------------------------------------ tensor-core path
+// One pipeline stage holds BPS consecutive KV blocks (K and V tiles) of one KV
+// head: kTok = BPS * BS token rows of D bf16/fp16 values, stored per 64-column
+// chunk as 128-byte rows with the TMA 128-byte swizzle.
 template <int D, int BS>
 struct MmaGeom {
-  static constexpr int kChunks = D / 64;          // 128-byte swizzle atoms per row
-  static constexpr int kTile = BS * D * 2;        // bytes of one K (or V) tile
-  static constexpr int kStage = 2 * kTile;        // K + V
-  static constexpr int kStages = (D >= 256) ? 2 : 3;
-  static constexpr int kPipeBytes = kNumWarps * kStages * kStage;
-  static constexpr int kRedBytes = kNumWarps * kMmaCols * (D + 4) * 4 + 2 * kNumWarps * kMmaCols * 4;
+  static constexpr int kChunks = D / 64;  // 128-byte swizzle atoms per row
+  static constexpr int kBps = (CLOVER_MMA_STAGE_TOKENS > BS ? CLOVER_MMA_STAGE_TOKENS : BS) / BS;
+  static constexpr int kTok = kBps * BS;   // tokens per stage
+  static constexpr int kTile = kTok * D * 2;
+  static constexpr int kStage = 2 * kTile;  // K + V
+  // keep the ring within the per-CTA shared memory limit
+  static constexpr int kStages = kMmaWarps * CLOVER_MMA_STAGES * kStage <= 200 * 1024
+                                     ? CLOVER_MMA_STAGES
+                                     : (kMmaWarps * 2 * kStage <= 200 * 1024 ? 2 : 1);
+  static constexpr int kPipeBytes = kMmaWarps * kStages * kStage;
+  static constexpr int kRedBytes = kMmaWarps * kMmaCols * (D + 4) * 4 + 2 * kMmaWarps * kMmaCols * 4;
   static constexpr int kSmem = (kPipeBytes > kRedBytes ? kPipeBytes : kRedBytes) + 1024;
-  static constexpr int kMaxBlocksPerCta = 32 * kNumWarps;  // one table id per lane per warp
+  static constexpr int kMaxGroupsPerWarp = 32;  // one lane holds the block ids of one group
 };
 
-// byte offset of 16-byte chunk `cg` (along head_dim) of tile row `r` (128B swizzle)
-template <int BS>
+// byte offset of 16-byte chunk `cg` (along head_dim) of stage row `r`
+template <int TOK>
 __device__ __forceinline__ uint32_t swz(int r, int cg) {
   const int c64 = cg >> 3, c = cg & 7;
-  return (uint32_t)(c64 * BS * 128 + r * 128 + ((c ^ (r & 7)) << 4));
+  return (uint32_t)(c64 * TOK * 128 + r * 128 + ((c ^ (r & 7)) << 4));
 }
 
 template <typename T, bool QF32, int D, int BS>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kMmaThreads, D >= 256 ? 1 : CLOVER_MMA_MIN_CTAS)
 paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const DecodeArgs a) {
   using G = MmaGeom<D, BS>;
+  constexpr int NW = kMmaWarps;
   constexpr int STAGES = G::kStages;
-  constexpr int MT = BS / 16;  // token m-tiles per block
-  constexpr int KK = D / 16;   // k-steps (QK) / m-tiles (PV) over head_dim
+  constexpr int BPS = G::kBps;
+  constexpr int TOK = G::kTok;
+  constexpr int MT = TOK / 16;  // token m-tiles per stage
+  constexpr int KK = D / 16;    // k-steps (QK) / m-tiles (PV) over head_dim
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[kNumWarps * STAGES];
+  __shared__ __align__(8) uint64_t bars[NW * STAGES];
   __shared__ int s_abort;
 
   CtaWork w;
@@ -230,8 +257,31 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
 
+  // Block ids of this CTA's partition, fetched before the barrier set-up so
+  // their latency overlaps it: lane j of warp w holds the BPS ids of the
+  // warp's j-th stage group (groups w, w+NW, ... of the partition).
+  const int blk0 = w.tok_begin / BS;
+  const int n_blk = (w.tok_end - w.tok_begin + BS - 1) / BS;
+  const int n_grp = (n_blk + BPS - 1) / BPS;
+  const int n_mine = warp < n_grp ? (n_grp - warp + NW - 1) / NW : 0;
+  int my_blk[BPS];
+#pragma unroll
+  for (int i = 0; i < BPS; ++i) {
+    my_blk[i] = -1;
+    const int gi = (warp + lane * NW) * BPS + i;  // block index within the partition
+    if (lane < n_mine && gi < n_blk) {
+      const int bi = blk0 + gi;
+      int id = bi < a.table_stride ? __ldg(w.tab + bi) : -1;
+      if (id < 0 || id >= a.num_blocks) {
+        raise_status(a.status, CLOVER_B200_DEV_BAD_BLOCK);
+        id = 0;  // keep the pipeline well-formed; the output is flagged invalid
+      }
+      my_blk[i] = id;
+    }
+  }
+
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kNumWarps * STAGES; ++i) mbar_init(smem_addr(&bars[i]), 1);
+    for (int i = 0; i < NW * STAGES; ++i) mbar_init(smem_addr(&bars[i]), 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmV);
@@ -239,34 +289,32 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   }
   __syncthreads();
 
-  const int blk0 = w.tok_begin / BS;
-  const int n_blk = (w.tok_end - w.tok_begin + BS - 1) / BS;
-  const int n_mine = warp < n_blk ? (n_blk - warp + kNumWarps - 1) / kNumWarps : 0;
-  int my_blk = 0;
-  if (lane < n_mine) {
-    const int bi = blk0 + warp + lane * kNumWarps;
-    int id = bi < a.table_stride ? __ldg(w.tab + bi) : -1;
-    if (id < 0 || id >= a.num_blocks) {
-      raise_status(a.status, CLOVER_B200_DEV_BAD_BLOCK);
-      id = 0;  // keep the pipeline well-formed; the output is flagged invalid
-    }
-    my_blk = id;
-  }
   const uint32_t ring = smem_addr(smem) + warp * STAGES * G::kStage;
   const uint32_t bar0 = smem_addr(&bars[warp * STAGES]);
 
+  // Fetch this warp's k-th stage group (all lanes call: the ids are shuffled).
   auto issue = [&](int k) {
-    const int id = __shfl_sync(0xffffffffu, my_blk, k);
+    int ids[BPS];
+#pragma unroll
+    for (int i = 0; i < BPS; ++i) ids[i] = __shfl_sync(0xffffffffu, my_blk[i], k);
     if (lane == 0) {
       const int s = k % STAGES;
       const uint32_t bar = bar0 + s * 8;
       const uint32_t kd = ring + s * G::kStage;
       const uint32_t vd = kd + G::kTile;
-      mbar_arrive_expect_tx(bar, G::kStage);
+      int nb = 0;
 #pragma unroll
-      for (int c = 0; c < G::kChunks; ++c) {
-        tma_load_3d(kd + c * BS * 128, &tmK, c * 64, w.kvh, id * BS, bar);
-        tma_load_3d(vd + c * BS * 128, &tmV, c * 64, w.kvh, id * BS, bar);
+      for (int i = 0; i < BPS; ++i) nb += ids[i] >= 0;
+      mbar_arrive_expect_tx(bar, nb * 2 * BS * D * 2);
+#pragma unroll
+      for (int i = 0; i < BPS; ++i) {
+        if (ids[i] < 0) continue;
+#pragma unroll
+        for (int c = 0; c < G::kChunks; ++c) {
+          const uint32_t off = c * TOK * 128 + i * BS * 128;
+          tma_load_3d(kd + off, &tmK, c * 64, w.kvh, ids[i] * BS, bar);
+          tma_load_3d(vd + off, &tmV, c * 64, w.kvh, ids[i] * BS, bar);
+        }
       }
     }
   };
@@ -305,15 +353,17 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
     lim_b = c1.valid ? c1.limit : 0;
   }
 
-  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
-  float acc[KK][4];
-#pragma unroll
-  for (int i = 0; i < KK; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-
+  // First stages: issued once the query and block-id loads are both in
+  // flight, so their latencies overlap.
   const int npre = n_mine < STAGES ? n_mine : STAGES;
   for (int k = 0; k < npre; ++k) issue(k);
   int issued = npre;
   int consumed = 0;
+
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+  float acc[KK][4];
+#pragma unroll
+  for (int i = 0; i < KK; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   bool timed_out = false;
 
   for (int k = 0; k < n_mine; ++k) {
@@ -325,35 +375,40 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
     consumed = k + 1;
     const uint32_t ks = ring + s * G::kStage;
     const uint32_t vs = ks + G::kTile;
-    const int tok0 = (blk0 + warp + k * kNumWarps) * BS;
+    const int tok0 = w.tok_begin + (warp + k * NW) * TOK;
     const int nvalid = w.tok_end - tok0;
-    if (nvalid < BS) {
-      // Rows past the end of the context may hold stale data: zero them in V
-      // so that P = 0 never multiplies a non-finite value.
+    if (nvalid < TOK) {
+      // Rows past the end of the context (stale data, or blocks not fetched)
+      // are zeroed in V so that P = 0 never multiplies a non-finite value.
       uint8_t* vg = smem + (vs - smem_addr(smem));
-      for (int idx = lane; idx < (BS - nvalid) * (D / 8); idx += 32) {
+      for (int idx = lane; idx < (TOK - nvalid) * (D / 8); idx += 32) {
         const int r = nvalid + idx / (D / 8);
-        const int cg = idx % (D / 8);
-        *reinterpret_cast<uint4*>(vg + swz<BS>(r, cg)) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(vg + swz<TOK>(r, idx % (D / 8))) = make_uint4(0, 0, 0, 0);
       }
       __syncwarp();
     }
 
-    // ---- S = K . Q^T (tokens x columns), fp32 accumulate
+    // ---- S = K . Q^T (tokens x columns): independent accumulator chains
+    // (even/odd k-steps, hi/lo query halves) summed at the end.
     float sc[MT][4];
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
-      sc[mt][0] = sc[mt][1] = sc[mt][2] = sc[mt][3] = 0.f;
+      float ch[QF32 ? 4 : 2][4];
+#pragma unroll
+      for (int c = 0; c < (QF32 ? 4 : 2); ++c) ch[c][0] = ch[c][1] = ch[c][2] = ch[c][3] = 0.f;
       const int r = mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
       for (int kk = 0; kk < KK; ++kk) {
         uint32_t a0, a1, a2, a3;
-        ldsm_x4(ks + swz<BS>(r, kk * 2 + (lane >> 4)), a0, a1, a2, a3);
-        MmaOp<T>::run(sc[mt], a0, a1, a2, a3, qh[kk][0], qh[kk][1]);
-        if (QF32) MmaOp<T>::run(sc[mt], a0, a1, a2, a3, ql[kk][0], ql[kk][1]);
+        ldsm_x4(ks + swz<TOK>(r, kk * 2 + (lane >> 4)), a0, a1, a2, a3);
+        MmaOp<T>::run(ch[kk & 1], a0, a1, a2, a3, qh[kk][0], qh[kk][1]);
+        if (QF32) MmaOp<T>::run(ch[2 + (kk & 1)], a0, a1, a2, a3, ql[kk][0], ql[kk][1]);
       }
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        sc[mt][e] = QF32 ? (ch[0][e] + ch[1][e]) + (ch[2][e] + ch[3][e]) : ch[0][e] + ch[1][e];
     }
-    // ---- scale (base-2 domain), causal mask, block max per column
+    // ---- scale (base-2 domain), causal mask, stage max per column
     float mx_a = -INFINITY, mx_b = -INFINITY;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
@@ -388,7 +443,7 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
       acc[i][2] *= al_a;
       acc[i][3] *= al_b;
     }
-    // ---- O^T += V^T . P^T
+    // ---- O^T += V^T . P^T  (P split hi + lo; V^T via ldmatrix.trans)
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
       const float p0 = fast_exp2(sc[mt][0] - u_a), p1 = fast_exp2(sc[mt][1] - u_b);
@@ -402,13 +457,16 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
       const uint32_t bl0 = movm_trans(l_top), bl1 = movm_trans(l_bot);
       const int grp = lane >> 3;
       const int r = mt * 16 + (lane & 7) + (grp >> 1) * 8;
+      uint32_t va[KK][4];
 #pragma unroll
-      for (int dm = 0; dm < KK; ++dm) {
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4_trans(vs + swz<BS>(r, dm * 2 + (grp & 1)), a0, a1, a2, a3);
-        MmaOp<T>::run(acc[dm], a0, a1, a2, a3, bh0, bh1);
-        MmaOp<T>::run(acc[dm], a0, a1, a2, a3, bl0, bl1);
-      }
+      for (int dm = 0; dm < KK; ++dm)
+        ldsm_x4_trans(vs + swz<TOK>(r, dm * 2 + (grp & 1)), va[dm][0], va[dm][1], va[dm][2], va[dm][3]);
+#pragma unroll
+      for (int dm = 0; dm < KK; ++dm)
+        MmaOp<T>::run(acc[dm], va[dm][0], va[dm][1], va[dm][2], va[dm][3], bh0, bh1);
+#pragma unroll
+      for (int dm = 0; dm < KK; ++dm)
+        MmaOp<T>::run(acc[dm], va[dm][0], va[dm][1], va[dm][2], va[dm][3], bl0, bl1);
     }
     __syncwarp();
     if (k + STAGES < n_mine) {
@@ -435,8 +493,8 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   if (s_abort) return;
 
   float* red_acc = reinterpret_cast<float*>(smem);
-  float* red_m = red_acc + kNumWarps * kMmaCols * (D + 4);
-  float* red_l = red_m + kNumWarps * kMmaCols;
+  float* red_m = red_acc + NW * kMmaCols * (D + 4);
+  float* red_l = red_m + NW * kMmaCols;
   {
     float* base = red_acc + (warp * kMmaCols) * (D + 4);
 #pragma unroll
@@ -455,7 +513,7 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
     }
   }
   __syncthreads();
-  merge_store_rt(a, w, red_acc, red_m, red_l, kMmaCols, D);
+  merge_store_rt(a, w, red_acc, red_m, red_l, kMmaCols, D, NW);
 }
 
 // ------------------------------------------------------------------ SIMT path
@@ -538,33 +596,84 @@ paged_decode_simt_kernel(const DecodeArgs a, int D) {
     }
   }
   __syncthreads();
-  merge_store_rt(a, w, red_acc, red_m, red_l, NC, D);
+  merge_store_rt(a, w, red_acc, red_m, red_l, NC, D, kNumWarps);
 }
 
 // ------------------------------------------------------------------ split-K reduce
-__global__ void __launch_bounds__(128)
+// One CTA (4 warps) per (query row, head).  The partitions' log-sum-exp
+// weights are computed once into shared memory; warp w sums partitions
+// w, w+4, ... with lanes covering EPL consecutive dims (float4 for D = 128);
+// the four warp sums are combined in shared memory.
+constexpr int kReduceWarps = 4;
+constexpr int kReduceMaxParts = 1024;
+
+template <int EPL>
+__global__ void __launch_bounds__(kReduceWarps * 32)
 splitk_reduce_kernel(const DecodeArgs a, int D) {
+  __shared__ float s_w[kReduceMaxParts];
+  __shared__ float s_red[kReduceWarps][32 * EPL];
+  __shared__ float s_wmax[kReduceWarps], s_wsum[kReduceWarps];
   const int r = blockIdx.x;
   const int h = blockIdx.y;
   const int lim = __ldg(a.ctx + r);
   const int np = (lim + a.part_tokens - 1) / a.part_tokens;
-  const int64_t obase = (int64_t)r * a.out_stride + (int64_t)h * D;
   if (np <= 1) return;  // written (or zero-filled) by the decode kernel
-  const int npp = np < a.max_parts ? np : a.max_parts;
+  const int npp = min(min(np, a.max_parts), kReduceMaxParts);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t base = ((int64_t)r * a.num_q_heads + h) * a.max_parts;
   const float* lse = a.part_lse + base;
+  // max and weights
   float M = -INFINITY;
-  for (int p = 0; p < npp; ++p) M = fmaxf(M, lse[p]);
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float L = 0.f, O = 0.f;
-    if (M != -INFINITY) {
-      for (int p = 0; p < npp; ++p) {
-        const float e = fast_exp2(lse[p] - M);
-        L += e;
-        O += e * a.part_out[(base + p) * D + d];
-      }
+  for (int p = threadIdx.x; p < npp; p += blockDim.x) M = fmaxf(M, lse[p]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  if (lane == 0) s_wmax[warp] = M;
+  __syncthreads();
+  M = fmaxf(fmaxf(s_wmax[0], s_wmax[1]), fmaxf(s_wmax[2], s_wmax[3]));
+  float L = 0.f;
+  for (int p = threadIdx.x; p < npp; p += blockDim.x) {
+    const float wt = M == -INFINITY ? 0.f : fast_exp2(lse[p] - M);
+    s_w[p] = wt;
+    L += wt;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+  if (lane == 0) s_wsum[warp] = L;
+  __syncthreads();
+  L = (s_wsum[0] + s_wsum[1]) + (s_wsum[2] + s_wsum[3]);
+  // weighted sum of the partial outputs
+  const int d0 = lane * EPL;
+  float o[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) o[e] = 0.f;
+  const float* po = a.part_out + base * D + d0;
+  if (EPL == 4 && D == 128) {
+#pragma unroll 4
+    for (int p = warp; p < npp; p += kReduceWarps) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(po + (int64_t)p * D));
+      const float wt = s_w[p];
+      o[0] = fmaf(wt, v.x, o[0]);
+      o[1] = fmaf(wt, v.y, o[1]);
+      o[2] = fmaf(wt, v.z, o[2]);
+      o[3] = fmaf(wt, v.w, o[3]);
     }
-    store_out(a, obase + d, L > 0.f ? O / L : 0.f);
+  } else {
+#pragma unroll 4
+    for (int p = warp; p < npp; p += kReduceWarps) {
+      const float wt = s_w[p];
+#pragma unroll
+      for (int e = 0; e < EPL; ++e)
+        if (d0 + e < D) o[e] = fmaf(wt, __ldcg(po + (int64_t)p * D + e), o[e]);
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) s_red[warp][d0 + e] = o[e];
+  __syncthreads();
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  const int64_t obase = (int64_t)r * a.out_stride + (int64_t)h * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    const float v = (s_red[0][d] + s_red[1][d]) + (s_red[2][d] + s_red[3][d]);
+    store_out(a, obase + d, v * inv);
   }
 }
 
@@ -625,15 +734,24 @@ static bool mma_supported(int kv_dtype, int q_dtype, int D, int BS) {
          (BS == 16 || BS == 32);
 }
 
+static int MmaGeomBps(int BS) {
+  return (CLOVER_MMA_STAGE_TOKENS > BS ? CLOVER_MMA_STAGE_TOKENS : BS) / BS;
+}
+// one lane per stage group and warp holds the group's block ids
+static int max_mma_partition(int BS) { return 32 * kMmaWarps * MmaGeomBps(BS) * BS; }
+
 static int choose_partition(int max_ctx, int BS, int rows_x_kvh, bool mma) {
   // 512-token partitions by default (flash-decoding split); shorter contexts
   // with few (row, head) units split finer so the grid still covers the GPU.
   int pt = 512;
-  const int min_pt = BS * kNumWarps;
-  while (pt > min_pt && (int64_t)rows_x_kvh * ((max_ctx + pt - 1) / pt) < 2 * 148) pt /= 2;
+  const int min_pt = BS * (mma ? kMmaWarps * MmaGeomBps(BS) : kNumWarps);
+  while (pt > min_pt && (int64_t)rows_x_kvh * ((max_ctx + pt - 1) / pt) < 2 * 148 &&
+         (max_ctx + pt / 2 - 1) / (pt / 2) <= kReduceMaxParts)
+    pt /= 2;
   if (pt < min_pt) pt = min_pt;
+  while ((max_ctx + pt - 1) / pt > kReduceMaxParts) pt *= 2;  // very long contexts
   pt = (pt + BS - 1) / BS * BS;
-  if (mma && pt > 32 * kNumWarps * BS) pt = 32 * kNumWarps * BS;
+  if (mma && pt > max_mma_partition(BS)) pt = max_mma_partition(BS);
   return pt;
 }
 
@@ -659,7 +777,7 @@ static int launch_mma(const DecodeArgs& a, const CUtensorMap& tk, const CUtensor
     if (rc) return rc;
     if (dev < 64) configured |= 1ull << dev;
   }
-  kern<<<grid, kThreads, G::kSmem, s>>>(tk, tv, a);
+  kern<<<grid, kMmaThreads, G::kSmem, s>>>(tk, tv, a);
   return check_cuda(cudaGetLastError(), "paged_decode_mma launch");
 }
 
@@ -743,12 +861,16 @@ static int make_plan(int n_seqs, int n_rows, int max_q, int max_ctx, int hq, int
   } else {
     if (pt % BS != 0)
       return set_error(CLOVER_B200_ERR_INVALID_ARG, "paged_decode: partition_tokens %% block_size != 0");
-    if (pl->mma && pt > 32 * kNumWarps * BS)
+    if (pl->mma && pt > max_mma_partition(BS))
       return set_error(CLOVER_B200_ERR_INVALID_ARG, "paged_decode: partition_tokens > %d",
-                       32 * kNumWarps * BS);
+                       max_mma_partition(BS));
   }
   pl->part_tokens = pt;
   pl->max_parts = max_ctx > 0 ? (max_ctx + pt - 1) / pt : 1;
+  if (pl->max_parts > kReduceMaxParts)
+    return set_error(CLOVER_B200_ERR_UNSUPPORTED,
+                     "paged_decode: %d partitions > %d (raise partition_tokens)", pl->max_parts,
+                     kReduceMaxParts);
   pl->workspace_bytes = workspace_bytes(n_rows, hq, D, pl->max_parts);
   return CLOVER_B200_OK;
 }
@@ -865,7 +987,16 @@ extern "C" int clover_b200_paged_decode(
   if (max_parts > 1) {
     // Rows with several partitions are combined here; single-partition rows
     // were written by the decode kernel and return at once.
-    splitk_reduce_kernel<<<dim3(n_query_rows, num_q_heads), 128, 0, s>>>(a, head_dim);
+    const dim3 rgrid(n_query_rows, num_q_heads);
+    const int rt = kReduceWarps * 32;
+    if (head_dim <= 32)
+      splitk_reduce_kernel<1><<<rgrid, rt, 0, s>>>(a, head_dim);
+    else if (head_dim <= 64)
+      splitk_reduce_kernel<2><<<rgrid, rt, 0, s>>>(a, head_dim);
+    else if (head_dim <= 128)
+      splitk_reduce_kernel<4><<<rgrid, rt, 0, s>>>(a, head_dim);
+    else
+      splitk_reduce_kernel<8><<<rgrid, rt, 0, s>>>(a, head_dim);
     rc = check_cuda(cudaGetLastError(), "splitk_reduce launch");
   }
   return rc;
