@@ -6,8 +6,8 @@ Under torchrun (N > 1) each rank owns Hkv/N KV heads (head sharding) and the
 step ends with an NCCL all-gather of the per-rank outputs.
 
 One "step" = one attention step of one layer for the whole batch at the
-configuration's context length: slot mapping -> KV append of the new token ->
-paged decode (split-K) -> split-K reduce (-> all-gather).  ``value`` times that
+configuration's context length: KV append of each sequence's new token fused
+with the paged decode (split-K) -> split-K reduce (-> all-gather).  ``value`` times that
 step on device-resident inputs (a CUDA graph replayed K times between CUDA
 events, max over ranks); ``e2e`` times the same step through the public
 ``B200AttentionBackend.decode_layer_batch`` API with host (pinned) inputs and
@@ -236,9 +236,11 @@ def build_step(cfg, rank, world, lens, device, seed=0):
                           status=pool.status)
 
     def step():
-        _lib.compute_slots(pool.tables, rows, pos, offs, bs, pool.num_blocks, slots, pool.status)
-        _lib.kv_append(pool.k[0], pool.v[0], kn, vn, slots, pool.status)
-        decode_only()
+        # append each sequence's new token at position ctx-1 and attend (fused)
+        _lib.decode_step(out, q, pool.k[0], pool.v[0], kn, vn, pool.tables, offs, ctx,
+                         max_queries_per_seq=1, max_ctx_len=max(lens), score_scale=cfg.score_scale,
+                         seq_rows=rows, partition_tokens=cfg.partition_tokens, workspace=ws,
+                         status=pool.status)
 
     return dict(pool=pool, q=q, out=out, step=step, decode_only=decode_only, hkv_local=hkv_l,
                 hq_local=hq_l, kv_range=(lo, hi))
@@ -270,7 +272,7 @@ def run_b200(args):
 
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
-    launches_per_step = 3 + (1 if _lib.decode_workspace_bytes(
+    launches_per_step = 1 + (1 if _lib.decode_workspace_bytes(
         B, B, 1, max(lens), st["hq_local"], st["hkv_local"], cfg.head_dim, cfg.block_size,
         cfg.dtype, torch.float32, cfg.partition_tokens) > 0 else 0)
 

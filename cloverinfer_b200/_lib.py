@@ -49,6 +49,9 @@ SIGNATURES = {
     "clover_b200_paged_decode": (ctypes.c_int, [
         _P, _I64, _P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _I32, _P, _P, _P,
         _I32, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _P, _P]),
+    "clover_b200_decode_step": (ctypes.c_int, [
+        _P, _I64, _P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _P, _I64, _P, _I32, _P, _P, _P,
+        _I32, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _P, _P]),
     "clover_b200_paged_decode_noalloc": (ctypes.c_int, [
         _P, _I64, _P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _I32, _P, _P, _P,
         _I32, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _P]),
@@ -208,3 +211,36 @@ def paged_decode(out, q, k_cache, v_cache, block_tables, query_start_loc, ctx_le
         float(score_scale), partition_tokens, _ptr(workspace), ws_bytes, _ptr(status),
         _stream(q.device))
     _check(rc, "clover_b200_paged_decode")
+
+
+def decode_step(out, q, k_cache, v_cache, k_new, v_new, block_tables, query_start_loc, ctx_lens, *,
+                max_queries_per_seq, max_ctx_len, score_scale, seq_rows=None,
+                partition_tokens=0, workspace=None, status=None):
+    """Append row r's new token (k_new/v_new[r], [n_rows, Hkv, D]) at ctx_lens[r]-1, then
+    paged decode as :func:`paged_decode` — one launch when the append can be fused."""
+    _require_cuda(out, q, k_cache, v_cache, k_new, v_new, block_tables, query_start_loc,
+                  ctx_lens, seq_rows, workspace, status)
+    nb, bs, hkv, d = k_cache.shape
+    rows, hq, dq = q.shape
+    if dq != d or out.shape != q.shape or out.dtype != q.dtype:
+        raise ValueError("decode_step: q/out mismatch")
+    if k_new.shape != (rows, hkv, d) or v_new.shape != k_new.shape:
+        raise ValueError(f"decode_step: new K/V must be [{rows}, {hkv}, {d}]")
+    if k_new.dtype != k_cache.dtype or v_new.dtype != k_cache.dtype:
+        raise TypeError("decode_step: new K/V dtype must match the cache")
+    if k_new.stride(2) != 1 or k_new.stride(1) != d or v_new.stride() != k_new.stride():
+        raise ValueError("decode_step: each token's [Hkv, D] row must be contiguous")
+    if q.stride(2) != 1 or q.stride(1) != d or out.stride(2) != 1 or out.stride(1) != d:
+        raise ValueError("decode_step: each row's [Hq, D] must be contiguous")
+    n_seqs = query_start_loc.numel() - 1
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    rc = lib().clover_b200_decode_step(
+        _ptr(out), out.stride(0), _ptr(q), q.stride(0), dtype_code(q.dtype),
+        _ptr(k_cache), _ptr(v_cache), dtype_code(k_cache.dtype), nb, bs,
+        _ptr(k_new), _ptr(v_new), k_new.stride(0),
+        _ptr(block_tables), block_tables.stride(0), _ptr(seq_rows), _ptr(query_start_loc),
+        _ptr(ctx_lens), n_seqs, rows, max_queries_per_seq, max_ctx_len, hq, hkv, d,
+        float(score_scale), partition_tokens, _ptr(workspace), ws_bytes, _ptr(status),
+        _stream(q.device))
+    _check(rc, "clover_b200_decode_step")
+

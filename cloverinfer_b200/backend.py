@@ -21,8 +21,9 @@ and on the query's device.
 Differences that are the point of the rewrite: the KV cache is paged in HBM
 (``PagedKVPool``) with native GQA (``Hkv`` heads stored, ``repeat_kv``-expanded
 K/V accepted and collapsed); the attention is the sm_100a kernel; a batch is
-one launch sequence (reserve -> slots -> append -> decode -> reduce) instead of
-a Python loop; KV heads can be sharded over GPUs (``HeadShardGroup``) with one
+one launch sequence (block reserve when a sequence crosses a block boundary,
+then one fused append + decode kernel, then the split-K reduce) instead of a
+Python loop; KV heads can be sharded over GPUs (``HeadShardGroup``) with one
 all-gather of the outputs.
 
 ``decode_batch`` is the tensor API for a step-batched engine
@@ -274,12 +275,8 @@ class B200AttentionBackend:
         for p, n in zip(pos, n_new):
             offs.append(offs[-1] + n)
             ctx_rows.extend(range(p + 1, p + n + 1))
-        meta = to_device_i32(rows + pos + offs + ctx_rows, self.device)
-        rows_d, pos_d = meta[0:B], meta[B:2 * B]
-        offs_d, ctx_d = meta[2 * B:3 * B + 1], meta[3 * B + 1:]
-
-        slots = pool.slots(rows_d, pos_d, offs_d, T)
-        pool.append(layer_idx, self._local_kv(key), self._local_kv(value), slots)
+        meta = to_device_i32(rows + offs + ctx_rows, self.device)
+        rows_d, offs_d, ctx_d = meta[0:B], meta[B:2 * B + 1], meta[2 * B + 1:]
 
         lo, hi = self.kv_range
         q = query.to(self.device, non_blocking=True)
@@ -289,8 +286,10 @@ class B200AttentionBackend:
             q = q[:, lo * group:hi * group]
         if q.stride(2) != 1 or q.stride(1) != self.head_dim:
             q = q.contiguous()
-        out = pool.decode(layer_idx, q, offs_d, ctx_d, rows_d, max(n_new), max(targets),
-                          score_scale, partition_tokens=self.partition_tokens)
+        # one launch: append each row's token at ctx - 1, then attend (+ reduce)
+        out = pool.decode_step(layer_idx, q, self._local_kv(key), self._local_kv(value), offs_d,
+                               ctx_d, rows_d, max(n_new), max(targets), score_scale,
+                               partition_tokens=self.partition_tokens)
         for r, n in zip(reqs, n_new):
             r.layer_len[layer_idx] += n
             if layer_idx == self.num_layers - 1:

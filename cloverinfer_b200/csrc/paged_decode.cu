@@ -84,6 +84,13 @@ struct DecodeArgs {
   float* part_out;
   float* part_lse;
   int32_t* status;
+  // Fused KV append (decode_step): row r's new token k_new/v_new[r] (all local
+  // KV heads, token stride new_stride elements) is written to position
+  // ctx[r] - 1 before attending.  Null when the caller appended already.
+  const void* k_new;
+  const void* v_new;
+  int64_t new_stride;
+  int32_t kv_esz;
 };
 
 struct ColInfo {
@@ -166,6 +173,70 @@ __device__ __forceinline__ bool cta_work(const DecodeArgs& a, CtaWork& w, int D)
   const int trow = a.seq_rows ? __ldg(a.seq_rows + w.b) : w.b;
   w.tab = a.tables + (int64_t)trow * a.table_stride;
   return true;
+}
+
+// Fused KV append: the CTA whose token range holds a row's new token writes
+// it (this CTA's KV head) into its paged slot.  Every CTA of a sequence has
+// the same column chunk when this is used, so each token has one writer and
+// nothing else reads that block before this CTA does.  Returns true if
+// anything was written (uniform across the CTA).
+__device__ __forceinline__ bool append_new_tokens(const DecodeArgs& a, const CtaWork& w, int D) {
+  const int vecs = D * a.kv_esz / 16;  // 16-byte vectors of one head row
+  bool wrote = false;
+  for (int j = 0; j < w.nq; ++j) {
+    const int pos = __ldg(a.ctx + w.row0 + j) - 1;
+    if (pos < w.tok_begin || pos >= w.tok_end) continue;
+    wrote = true;
+    const int bi = pos / a.block_size;
+    const int blk = bi < a.table_stride ? __ldg(w.tab + bi) : -1;
+    if (blk < 0 || blk >= a.num_blocks) {
+      if (threadIdx.x == 0) raise_status(a.status, CLOVER_B200_DEV_BAD_BLOCK);
+      continue;
+    }
+    const int64_t slot = (int64_t)blk * a.block_size + (pos - bi * a.block_size);
+    const int64_t src = (((int64_t)(w.row0 + j)) * a.new_stride + (int64_t)w.kvh * D) * a.kv_esz / 16;
+    const int64_t dst = ((slot * a.num_kv_heads + w.kvh) * D) * a.kv_esz / 16;
+    const uint4* ks = static_cast<const uint4*>(a.k_new) + src;
+    const uint4* vs = static_cast<const uint4*>(a.v_new) + src;
+    uint4* kd = static_cast<uint4*>(const_cast<void*>(a.k_cache)) + dst;
+    uint4* vd = static_cast<uint4*>(const_cast<void*>(a.v_cache)) + dst;
+    for (int v = threadIdx.x; v < 2 * vecs; v += blockDim.x) {
+      if (v < vecs) kd[v] = __ldg(ks + v);
+      else vd[v - vecs] = __ldg(vs + (v - vecs));
+    }
+  }
+  return wrote;
+}
+
+// Stand-alone append of every row's new token at ctx - 1 (one CTA per
+// sequence, all local KV heads) for launches that cannot fuse it.
+__global__ void __launch_bounds__(128)
+append_at_ctx_kernel(const DecodeArgs a, int D) {
+  const int b = blockIdx.x;
+  const int row0 = __ldg(a.qsl + b), nq = __ldg(a.qsl + b + 1) - row0;
+  const int trow = a.seq_rows ? __ldg(a.seq_rows + b) : b;
+  const int32_t* tab = a.tables + (int64_t)trow * a.table_stride;
+  const int esz = a.kv_esz;
+  const int64_t row_elems = (int64_t)a.num_kv_heads * D;
+  for (int j = 0; j < nq; ++j) {
+    const int pos = __ldg(a.ctx + row0 + j) - 1;
+    if (pos < 0) continue;
+    const int bi = pos / a.block_size;
+    const int blk = bi < a.table_stride ? __ldg(tab + bi) : -1;
+    if (blk < 0 || blk >= a.num_blocks) {
+      if (threadIdx.x == 0) raise_status(a.status, CLOVER_B200_DEV_BAD_BLOCK);
+      continue;
+    }
+    const int64_t slot = (int64_t)blk * a.block_size + (pos - bi * a.block_size);
+    const char* ks = static_cast<const char*>(a.k_new) + (int64_t)(row0 + j) * a.new_stride * esz;
+    const char* vs = static_cast<const char*>(a.v_new) + (int64_t)(row0 + j) * a.new_stride * esz;
+    char* kd = static_cast<char*>(const_cast<void*>(a.k_cache)) + slot * row_elems * esz;
+    char* vd = static_cast<char*>(const_cast<void*>(a.v_cache)) + slot * row_elems * esz;
+    for (int64_t e = threadIdx.x; e < row_elems * esz; e += blockDim.x) {
+      kd[e] = ks[e];
+      vd[e] = vs[e];
+    }
+  }
 }
 
 // Merge per-warp (m, l, O) partial states held in shared memory and store
@@ -252,6 +323,7 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
 
   CtaWork w;
   if (!cta_work(a, w, D)) return;
+  if (a.k_new != nullptr && append_new_tokens(a, w, D)) fence_proxy_async_global();
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int lane = threadIdx.x & 31;
@@ -526,6 +598,7 @@ paged_decode_simt_kernel(const DecodeArgs a, int D) {
   __shared__ float red_m[kNumWarps * NC], red_l[kNumWarps * NC];
   CtaWork w;
   if (!cta_work(a, w, D)) return;
+  if (a.k_new != nullptr && append_new_tokens(a, w, D)) __syncthreads();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int d0 = lane * EPL;
@@ -890,10 +963,13 @@ extern "C" int64_t clover_b200_decode_workspace_bytes(
   return pl.workspace_bytes;
 }
 
-extern "C" int clover_b200_paged_decode(
+// Shared body of paged_decode (k_new == nullptr) and decode_step (fused or
+// preceding KV append of every row's new token).
+static int decode_impl(
     void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride, int32_t q_dtype,
     const void* k_cache, const void* v_cache, int32_t kv_dtype, int64_t num_blocks,
-    int32_t block_size, const int32_t* block_tables, int32_t table_stride,
+    int32_t block_size, const void* k_new, const void* v_new, int64_t new_token_stride,
+    const int32_t* block_tables, int32_t table_stride,
     const int32_t* seq_rows, const int32_t* query_start_loc, const int32_t* ctx_lens,
     int32_t n_seqs, int32_t n_query_rows, int32_t max_queries_per_seq, int32_t max_ctx_len,
     int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, float score_scale,
@@ -958,8 +1034,33 @@ extern "C" int clover_b200_paged_decode(
                                                             max_parts * head_dim * 4))
                         : nullptr;
   a.status = dev_status;
+  a.k_new = nullptr;
+  a.v_new = nullptr;
+  a.new_stride = new_token_stride;
+  a.kv_esz = kv_dtype == CLOVER_B200_F32 ? 4 : 2;
 
   cudaStream_t s = (cudaStream_t)stream;
+  if (k_new != nullptr) {
+    if (!v_new || new_token_stride < (int64_t)num_kv_heads * head_dim)
+      return set_error(CLOVER_B200_ERR_INVALID_ARG, "decode_step: bad new K/V");
+    a.k_new = k_new;
+    a.v_new = v_new;
+    const bool fusable = col_chunks == 1 && (head_dim * a.kv_esz) % 16 == 0 &&
+                         (new_token_stride * a.kv_esz) % 16 == 0 &&
+                         !(reinterpret_cast<uintptr_t>(k_new) & 15) &&
+                         !(reinterpret_cast<uintptr_t>(v_new) & 15) &&
+                         !(reinterpret_cast<uintptr_t>(k_cache) & 15) &&
+                         !(reinterpret_cast<uintptr_t>(v_cache) & 15);
+    if (!fusable) {
+      // Several column chunks would read a new token's block before its one
+      // writer wrote it: append first in a kernel of its own.
+      append_at_ctx_kernel<<<n_seqs, 128, 0, s>>>(a, head_dim);
+      rc = check_cuda(cudaGetLastError(), "append_at_ctx launch");
+      if (rc) return rc;
+      a.k_new = nullptr;
+      a.v_new = nullptr;
+    }
+  }
   const dim3 grid(max_parts, num_kv_heads * col_chunks, n_seqs);
   if (mma) {
     CUtensorMap tk, tv;
@@ -1000,4 +1101,38 @@ extern "C" int clover_b200_paged_decode(
     rc = check_cuda(cudaGetLastError(), "splitk_reduce launch");
   }
   return rc;
+}
+
+extern "C" int clover_b200_paged_decode(
+    void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride, int32_t q_dtype,
+    const void* k_cache, const void* v_cache, int32_t kv_dtype, int64_t num_blocks,
+    int32_t block_size, const int32_t* block_tables, int32_t table_stride,
+    const int32_t* seq_rows, const int32_t* query_start_loc, const int32_t* ctx_lens,
+    int32_t n_seqs, int32_t n_query_rows, int32_t max_queries_per_seq, int32_t max_ctx_len,
+    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, float score_scale,
+    int32_t partition_tokens, void* workspace, int64_t workspace_bytes_, int32_t* dev_status,
+    void* stream) {
+  return decode_impl(out, out_row_stride, q, q_row_stride, q_dtype, k_cache, v_cache, kv_dtype,
+                     num_blocks, block_size, nullptr, nullptr, 0, block_tables, table_stride,
+                     seq_rows, query_start_loc, ctx_lens, n_seqs, n_query_rows,
+                     max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads, head_dim,
+                     score_scale, partition_tokens, workspace, workspace_bytes_, dev_status, stream);
+}
+
+extern "C" int clover_b200_decode_step(
+    void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride, int32_t q_dtype,
+    void* k_cache, void* v_cache, int32_t kv_dtype, int64_t num_blocks, int32_t block_size,
+    const void* k_new, const void* v_new, int64_t new_token_stride,
+    const int32_t* block_tables, int32_t table_stride, const int32_t* seq_rows,
+    const int32_t* query_start_loc, const int32_t* ctx_lens, int32_t n_seqs,
+    int32_t n_query_rows, int32_t max_queries_per_seq, int32_t max_ctx_len, int32_t num_q_heads,
+    int32_t num_kv_heads, int32_t head_dim, float score_scale, int32_t partition_tokens,
+    void* workspace, int64_t workspace_bytes_, int32_t* dev_status, void* stream) {
+  if (!k_new || !v_new)
+    return set_error(CLOVER_B200_ERR_INVALID_ARG, "decode_step: null new K/V");
+  return decode_impl(out, out_row_stride, q, q_row_stride, q_dtype, k_cache, v_cache, kv_dtype,
+                     num_blocks, block_size, k_new, v_new, new_token_stride, block_tables,
+                     table_stride, seq_rows, query_start_loc, ctx_lens, n_seqs, n_query_rows,
+                     max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads, head_dim,
+                     score_scale, partition_tokens, workspace, workspace_bytes_, dev_status, stream);
 }

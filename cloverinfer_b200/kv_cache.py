@@ -169,6 +169,25 @@ class PagedKVPool:
                           status=self.status)
         return out
 
+    def decode_step(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                    query_start_loc: torch.Tensor, ctx_lens: torch.Tensor,
+                    seq_rows: Optional[torch.Tensor], max_q: int, max_ctx: int, score_scale: float,
+                    out: Optional[torch.Tensor] = None, partition_tokens: int = 0) -> torch.Tensor:
+        """Append every query row's new token at ctx - 1 and attend (one fused
+        launch for a plain decode step).  Capacity must be reserved first."""
+        if out is None:
+            out = torch.empty_like(q)
+        n_seqs = query_start_loc.numel() - 1
+        nbytes = _lib.decode_workspace_bytes(n_seqs, q.shape[0], max_q, max_ctx, q.shape[1],
+                                             self.num_kv_heads, self.head_dim, self.block_size,
+                                             self.dtype, q.dtype, partition_tokens)
+        _lib.decode_step(out, q, self.k[layer], self.v[layer], k_new, v_new, self.tables,
+                         query_start_loc, ctx_lens, max_queries_per_seq=max_q, max_ctx_len=max_ctx,
+                         score_scale=score_scale, seq_rows=seq_rows,
+                         partition_tokens=partition_tokens, workspace=self.workspace(nbytes),
+                         status=self.status)
+        return out
+
     # ------------------------------------------------------------ checks / views
     def check_status(self) -> None:
         """Raise if any kernel flagged a bad index since the last check (syncs)."""

@@ -158,7 +158,8 @@ CLOVER_B200_API int64_t clover_b200_decode_workspace_bytes(int32_t n_seqs, int32
  *
  * score_scale is applied by the kernel (q may be pre-scaled, as OPT does
  * upstream: model_adapter.py:373, :386).  partition_tokens = 0 lets the
- * library pick the split; workspace must hold
+ * library pick the split; an explicit value must be a multiple of
+ * block_size and at most 64 * block_size on the tensor-core path; workspace must hold
  * clover_b200_decode_workspace_bytes(...) bytes (device) — it may be NULL
  * when every context fits in one partition.  Within a call, zero-length
  * contexts produce zeros.
@@ -170,6 +171,34 @@ CLOVER_B200_API int clover_b200_paged_decode(void* out, int64_t out_row_stride,
                              const void* q, int64_t q_row_stride, int32_t q_dtype,
                              const void* k_cache, const void* v_cache, int32_t kv_dtype,
                              int64_t num_blocks, int32_t block_size,
+                             const int32_t* block_tables, int32_t table_stride,
+                             const int32_t* seq_rows, const int32_t* query_start_loc,
+                             const int32_t* ctx_lens, int32_t n_seqs, int32_t n_query_rows,
+                             int32_t max_queries_per_seq, int32_t max_ctx_len,
+                             int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                             float score_scale, int32_t partition_tokens,
+                             void* workspace, int64_t workspace_bytes,
+                             int32_t* dev_status, void* stream);
+
+/*
+ * One attention step: KV append fused with paged decode.  Query row r brings
+ * one new token, k_new/v_new[r] ([num_kv_heads, head_dim], token stride
+ * new_token_stride elements, kv_dtype); it is written to position
+ * ctx_lens[r] - 1 of its sequence (the block table must already cover that
+ * position) and then every row attends exactly as clover_b200_paged_decode.
+ * When a sequence's columns (rows x GQA group) fit one CTA (the usual decode
+ * step) the append happens inside the decode kernel — the CTA owning the
+ * token's partition writes it before its TMA loads — otherwise a separate
+ * append kernel runs first.  Same workspace as clover_b200_paged_decode.
+ * Replaces: the append-then-attend of CpuAttentionBackend.decode_layer
+ * (attention_backend.py:105-118) and AttnPartition's write_new_kv + attention
+ * (src/core/graph_compiler.py:115-122).
+ */
+CLOVER_B200_API int clover_b200_decode_step(void* out, int64_t out_row_stride,
+                             const void* q, int64_t q_row_stride, int32_t q_dtype,
+                             void* k_cache, void* v_cache, int32_t kv_dtype,
+                             int64_t num_blocks, int32_t block_size,
+                             const void* k_new, const void* v_new, int64_t new_token_stride,
                              const int32_t* block_tables, int32_t table_stride,
                              const int32_t* seq_rows, const int32_t* query_start_loc,
                              const int32_t* ctx_lens, int32_t n_seqs, int32_t n_query_rows,

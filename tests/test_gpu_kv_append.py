@@ -86,3 +86,51 @@ def test_compute_slots_matches_upstream_arithmetic():
         want += [ref.slot(f"s{r}", n + j) for j in range(k)]
     assert slots == want
     pool.check_status()
+
+
+@pytest.mark.parametrize("dt,D,bs,n_new,hq,hkv", [(torch.bfloat16, 128, 16, [1, 1, 1, 1], 32, 8),
+                                                  (torch.float16, 128, 32, [1, 3, 4, 2], 32, 8),
+                                                  (torch.float32, 64, 16, [1, 1, 2], 12, 12),
+                                                  (torch.bfloat16, 64, 16, [2, 1, 1], 8, 2)])
+def test_decode_step_matches_append_then_decode(dt, D, bs, n_new, hq, hkv):
+    """clover_b200_decode_step (fused append, or its separate-append fallback
+    when a sequence's columns span several CTAs) == kv_append + paged_decode:
+    same cache bytes, same outputs."""
+    import math
+    from cloverinfer_b200 import _lib
+    from cloverinfer_b200.kv_cache import PagedKVPool
+    lens = [700, 33, 1500, 16][:len(n_new)]
+    outs, caches = [], []
+    for fused in (True, False):
+        g = torch.Generator().manual_seed(sum(n_new) + D)
+        pool = PagedKVPool(400, bs, hkv, D, dtype=dt, device="cuda", max_seqs=8, max_blocks_per_seq=128)
+        pool.shuffle_free_stack(5)
+        rows = list(range(len(lens)))
+        pool.reserve(rows, [n + k for n, k in zip(lens, n_new)])
+        gg = torch.Generator(device="cuda").manual_seed(1)
+        pool.k.normal_(generator=gg) if dt == torch.float32 else pool.k.copy_(torch.randn(pool.k.shape, generator=gg, device="cuda").to(dt))
+        pool.v.copy_(torch.randn(pool.v.shape, generator=gg, device="cuda").to(dt))
+        T = sum(n_new)
+        q = torch.randn(T, hq, D, generator=g).to(dt).float().cuda()
+        kn = torch.randn(T, hkv, D, generator=g).to(dt).cuda()
+        vn = torch.randn(T, hkv, D, generator=g).to(dt).cuda()
+        offs, ctx = [0], []
+        for n, k in zip(lens, n_new):
+            offs.append(offs[-1] + k)
+            ctx += list(range(n + 1, n + k + 1))
+        dev = "cuda"
+        rows_d = torch.tensor(rows, dtype=torch.int32, device=dev)
+        offs_d = torch.tensor(offs, dtype=torch.int32, device=dev)
+        ctx_d = torch.tensor(ctx, dtype=torch.int32, device=dev)
+        if fused:
+            out = pool.decode_step(0, q, kn, vn, offs_d, ctx_d, rows_d, max(n_new), max(ctx), 1 / math.sqrt(D))
+        else:
+            slots = pool.slots(rows_d, torch.tensor(lens, dtype=torch.int32, device=dev), offs_d, T)
+            pool.append(0, kn, vn, slots)
+            out = pool.decode(0, q, offs_d, ctx_d, rows_d, max(n_new), max(ctx), 1 / math.sqrt(D))
+        torch.cuda.synchronize()
+        pool.check_status()
+        outs.append(out.cpu())
+        caches.append((pool.k.cpu(), pool.v.cpu()))
+    assert torch.equal(caches[0][0], caches[1][0]) and torch.equal(caches[0][1], caches[1][1])
+    assert torch.equal(outs[0], outs[1])
