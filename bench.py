@@ -220,30 +220,33 @@ def build_step(cfg, rank, world, lens, device, seed=0):
     q = (torch.randn((B, hq_l, D), generator=g, device=device) * cfg.value_scale).to(dt).float()
     kn = (torch.randn((B, hkv_l, D), generator=g, device=device) * cfg.value_scale).to(dt)
     vn = (torch.randn((B, hkv_l, D), generator=g, device=device) * cfg.value_scale).to(dt)
+    # the configuration's split at N=1; with fewer KV heads per GPU the
+    # library's own choice keeps two waves of CTAs on the GPU
+    pt = cfg.partition_tokens if world == 1 else 0
+    pt = _lib.decode_partition_tokens(B, B, 1, max(lens), hq_l, hkv_l, D, bs, dt, torch.float32, pt)
     meta = torch.tensor(list(range(B)) + [n - 1 for n in lens] + list(range(B + 1)) + list(lens),
                         dtype=torch.int32, device=device)
     rows, pos, offs, ctx = meta[:B], meta[B:2 * B], meta[2 * B:3 * B + 1], meta[3 * B + 1:]
     slots = torch.empty(B, dtype=torch.int64, device=device)
     out = torch.empty_like(q)
-    nbytes = _lib.decode_workspace_bytes(B, B, 1, max(lens), hq_l, hkv_l, D, bs, dt, q.dtype,
-                                         cfg.partition_tokens)
+    nbytes = _lib.decode_workspace_bytes(B, B, 1, max(lens), hq_l, hkv_l, D, bs, dt, q.dtype, pt)
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
 
     def decode_only():
         _lib.paged_decode(out, q, pool.k[0], pool.v[0], pool.tables, offs, ctx,
                           max_queries_per_seq=1, max_ctx_len=max(lens), score_scale=cfg.score_scale,
-                          seq_rows=rows, partition_tokens=cfg.partition_tokens, workspace=ws,
+                          seq_rows=rows, partition_tokens=pt, workspace=ws,
                           status=pool.status)
 
     def step():
         # append each sequence's new token at position ctx-1 and attend (fused)
         _lib.decode_step(out, q, pool.k[0], pool.v[0], kn, vn, pool.tables, offs, ctx,
                          max_queries_per_seq=1, max_ctx_len=max(lens), score_scale=cfg.score_scale,
-                         seq_rows=rows, partition_tokens=cfg.partition_tokens, workspace=ws,
+                         seq_rows=rows, partition_tokens=pt, workspace=ws,
                          status=pool.status)
 
     return dict(pool=pool, q=q, out=out, step=step, decode_only=decode_only, hkv_local=hkv_l,
-                hq_local=hq_l, kv_range=(lo, hi))
+                hq_local=hq_l, kv_range=(lo, hi), partition_tokens=pt, workspace_bytes=nbytes)
 
 
 def run_b200(args):
@@ -272,9 +275,7 @@ def run_b200(args):
 
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
-    launches_per_step = 1 + (1 if _lib.decode_workspace_bytes(
-        B, B, 1, max(lens), st["hq_local"], st["hkv_local"], cfg.head_dim, cfg.block_size,
-        cfg.dtype, torch.float32, cfg.partition_tokens) > 0 else 0)
+    launches_per_step = 1 + (1 if st["workspace_bytes"] > 0 else 0)
 
     def full_step():
         st["step"]()
@@ -335,7 +336,13 @@ def run_b200(args):
     clk = clocks.stop()
     st["pool"].check_status()
     used_graph = graph is not None
-    del graph, dec_graph
+    # Release every graph (one may hold NCCL work) before anything else: a
+    # live graph with NCCL calls makes destroy_process_group wait for good.
+    if graph is not None:
+        graph.reset()
+    dec_graph.reset()
+    del run, graph, dec_graph
+    torch.cuda.synchronize(device)
 
     # ---------------- e2e through the public API (host buffers in, host out)
     e2e = run_e2e(cfg, lens, rank, world, device, args)
@@ -352,7 +359,7 @@ def run_b200(args):
         "config": {"workload": cfg.name, "batch": B, "ctx": f"{cfg.ctx_lo}-{cfg.ctx_hi}",
                    "num_q_heads": cfg.num_q_heads, "num_kv_heads": cfg.num_kv_heads,
                    "head_dim": cfg.head_dim, "block_size": cfg.block_size,
-                   "partition_tokens": cfg.partition_tokens,
+                   "partition_tokens": st["partition_tokens"],
                    "parallelism": f"kv-head-shard{world}", "cuda_graph": used_graph,
                    "l2": "inputs > L2 (KV %.0f MB per GPU)" % (local_kv / 1e6)},
         "steps_per_s": round(1e3 / ms, 2),
@@ -376,6 +383,7 @@ def run_b200(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
+        torch.cuda.synchronize(device)
         dist.barrier()
         dist.destroy_process_group()
 
@@ -390,7 +398,8 @@ def run_e2e(cfg, lens, rank, world, device, args):
                                              for n in lens) + 64,
                               block_size=cfg.block_size, num_kv_heads=cfg.num_kv_heads, kv_dtype=dt,
                               device=device, max_seqs=B, shard=shard, shuffle_seed=77,
-                              partition_tokens=cfg.partition_tokens, max_seq_len=max(lens) + 4096)
+                              partition_tokens=cfg.partition_tokens if world == 1 else 0,
+                              max_seq_len=max(lens) + 4096)
     g = torch.Generator(device=device).manual_seed(99)
     lo, hi = (0, cfg.num_kv_heads) if shard is None else shard.kv_range(cfg.num_kv_heads)
     for i, n in enumerate(lens):

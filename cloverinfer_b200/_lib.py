@@ -46,6 +46,7 @@ SIGNATURES = {
     "clover_b200_compute_slots": (ctypes.c_int, [_P, _I32, _P, _P, _P, _I32, _I32, _I64, _P, _P, _P]),
     "clover_b200_kv_append": (ctypes.c_int, [_P, _P, _P, _P, _I64, _P, _I64, _I32, _I32, _I32, _I64, _I32, _P, _P]),
     "clover_b200_decode_workspace_bytes": (ctypes.c_int64, [_I32] * 11),
+    "clover_b200_decode_partition_tokens": (ctypes.c_int, [_I32] * 11),
     "clover_b200_paged_decode": (ctypes.c_int, [
         _P, _I64, _P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _I32, _P, _P, _P,
         _I32, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _P, _P]),
@@ -182,6 +183,16 @@ def decode_workspace_bytes(n_seqs, n_rows, max_queries_per_seq, max_ctx_len, num
     if nb < 0:
         raise CloverB200Error(lib().clover_b200_last_error().decode(errors="replace"))
     return nb
+
+
+def decode_partition_tokens(n_seqs, n_rows, max_queries_per_seq, max_ctx_len, num_q_heads,
+                            num_kv_heads, head_dim, block_size, kv_dtype, q_dtype,
+                            partition_tokens=0) -> int:
+    pt = int(lib().clover_b200_decode_partition_tokens(
+        n_seqs, n_rows, max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads, head_dim,
+        block_size, dtype_code(kv_dtype), dtype_code(q_dtype), partition_tokens))
+    _check(OK if pt > 0 else pt, "clover_b200_decode_partition_tokens")
+    return pt
 
 
 def paged_decode(out, q, k_cache, v_cache, block_tables, query_start_loc, ctx_lens, *,

@@ -818,7 +818,9 @@ static int choose_partition(int max_ctx, int BS, int rows_x_kvh, bool mma) {
   // with few (row, head) units split finer so the grid still covers the GPU.
   int pt = 512;
   const int min_pt = BS * (mma ? kMmaWarps * MmaGeomBps(BS) : kNumWarps);
-  while (pt > min_pt && (int64_t)rows_x_kvh * ((max_ctx + pt - 1) / pt) < 2 * 148 &&
+  // two waves of the tensor-core kernel's resident CTAs (148 SMs)
+  const int64_t want = 2 * 148 * (mma ? CLOVER_MMA_MIN_CTAS : 4);
+  while (pt > min_pt && (int64_t)rows_x_kvh * ((max_ctx + pt - 1) / pt) < want &&
          (max_ctx + pt / 2 - 1) / (pt / 2) <= kReduceMaxParts)
     pt /= 2;
   if (pt < min_pt) pt = min_pt;
@@ -951,6 +953,17 @@ static int make_plan(int n_seqs, int n_rows, int max_q, int max_ctx, int hq, int
 }  // namespace clover
 
 using namespace clover;
+
+extern "C" int clover_b200_decode_partition_tokens(
+    int32_t n_seqs, int32_t n_query_rows, int32_t max_queries_per_seq, int32_t max_ctx_len,
+    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+    int32_t kv_dtype, int32_t q_dtype, int32_t partition_tokens) {
+  DecodePlan pl;
+  const int rc = make_plan(n_seqs, n_query_rows, max_queries_per_seq, max_ctx_len, num_q_heads,
+                           num_kv_heads, head_dim, block_size, kv_dtype, q_dtype,
+                           partition_tokens, &pl);
+  return rc ? rc : pl.part_tokens;
+}
 
 extern "C" int64_t clover_b200_decode_workspace_bytes(
     int32_t n_seqs, int32_t n_query_rows, int32_t max_queries_per_seq, int32_t max_ctx_len,

@@ -46,8 +46,9 @@ class HeadShardGroup:
         if hl != wmax:  # uneven split: pad to the widest shard
             send = torch.zeros((T, wmax, D), dtype=out_local.dtype, device=out_local.device)
             send[:, :hl] = out_local
-        recv = torch.empty((self.world, T, wmax, D), dtype=out_local.dtype, device=out_local.device)
+        recv = torch.empty((self.world * T, wmax, D), dtype=out_local.dtype, device=out_local.device)
         dist.all_gather_into_tensor(recv, send.contiguous(), group=self.pg)
+        recv = recv.view(self.world, T, wmax, D)
         if all(w == wmax for w in widths):
             return recv.permute(1, 0, 2, 3).reshape(T, self.world * wmax, D)
         return torch.cat([recv[r, :, :w] for r, w in enumerate(widths)], dim=1)

@@ -142,6 +142,17 @@ CLOVER_B200_API int64_t clover_b200_decode_workspace_bytes(int32_t n_seqs, int32
                                            int32_t q_dtype, int32_t partition_tokens);
 
 /*
+ * The split-K partition length (tokens) clover_b200_paged_decode uses for a
+ * call with these sizes (the library's choice when partition_tokens = 0), or
+ * a negative error code.
+ */
+CLOVER_B200_API int clover_b200_decode_partition_tokens(int32_t n_seqs, int32_t n_query_rows,
+                                           int32_t max_queries_per_seq, int32_t max_ctx_len,
+                                           int32_t num_q_heads, int32_t num_kv_heads,
+                                           int32_t head_dim, int32_t block_size, int32_t kv_dtype,
+                                           int32_t q_dtype, int32_t partition_tokens);
+
+/*
  * Paged decode attention with GQA and split-K (flash-decoding).
  *
  * Batch of n_seqs sequences; sequence b owns query rows

@@ -64,4 +64,3 @@ def test_sources_target_sm100a_only():
              if f.endswith((".cu", ".cuh"))]
     srcs = "".join(open(p).read() for p in files)
     assert "cp.async.bulk.tensor" in srcs and "mma.sync" in srcs
-    assert "." + "multicast" + "::cluster" not in srcs
