@@ -167,7 +167,7 @@ block_free_kernel(int32_t* __restrict__ free_stack, int32_t* __restrict__ free_t
   if (tid == 0) *free_top = top + s_total;
 }
 
-// One CTA per item; its threads cover the item's new tokens.
+// gridDim.y CTAs per item (x = item); their threads cover the item's new tokens.
 __global__ void __launch_bounds__(128)
 compute_slots_kernel(const int32_t* __restrict__ tables, int32_t stride,
                      const int32_t* __restrict__ rows, const int32_t* __restrict__ positions,
@@ -177,7 +177,8 @@ compute_slots_kernel(const int32_t* __restrict__ tables, int32_t stride,
   const int32_t* tab = tables + (int64_t)rows[i] * stride;
   const int32_t pos0 = positions[i];
   const int32_t t0 = offsets[i], t1 = offsets[i + 1];
-  for (int32_t t = t0 + threadIdx.x; t < t1; t += blockDim.x) {
+  const int32_t step = blockDim.x * gridDim.y;
+  for (int32_t t = t0 + blockIdx.y * blockDim.x + threadIdx.x; t < t1; t += step) {
     const int32_t pos = pos0 + (t - t0);
     const int32_t bi = pos / bs;
     int64_t slot = -1;
@@ -242,7 +243,10 @@ extern "C" int clover_b200_compute_slots(const int32_t* block_tables, int32_t ta
   if (n_items == 0) return CLOVER_B200_OK;
   if (!block_tables || !rows || !positions || !token_offsets || !slot_mapping)
     return set_error(CLOVER_B200_ERR_INVALID_ARG, "compute_slots: null pointer");
-  compute_slots_kernel<<<n_items, 128, 0, (cudaStream_t)stream>>>(
+  // a few CTAs per item so prefill-sized items (tens of thousands of tokens)
+  // are not a single CTA's serial loop
+  const int per_item = n_items >= 1024 ? 1 : 16;
+  compute_slots_kernel<<<dim3(n_items, per_item), 128, 0, (cudaStream_t)stream>>>(
       block_tables, table_stride, rows, positions, token_offsets, block_size, num_blocks,
       slot_mapping, dev_status);
   return check_cuda(cudaGetLastError(), "compute_slots launch");
