@@ -198,7 +198,7 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------ B200 arm
-def build_step(cfg, rank, world, lens, device, seed=0):
+def build_step(cfg, rank, world, lens, device, seed=0, gather=None):
     """Pool + static buffers for one decode step at the configured contexts."""
     from cloverinfer_b200 import _lib
     from cloverinfer_b200.head_groups import kv_head_shards
@@ -229,7 +229,11 @@ def build_step(cfg, rank, world, lens, device, seed=0):
     rows, pos, offs, ctx = meta[:B], meta[B:2 * B], meta[2 * B:3 * B + 1], meta[3 * B + 1:]
     slots = torch.empty(B, dtype=torch.int64, device=device)
     out = torch.empty_like(q)
-    nbytes = _lib.decode_workspace_bytes(B, B, 1, max(lens), hq_l, hkv_l, D, bs, dt, q.dtype, pt)
+    if gather is not None:
+        nbytes = _lib.decode_gather_workspace_bytes(B, B, 1, max(lens), hq_l, hkv_l, D, bs, dt,
+                                                    q.dtype, pt)
+    else:
+        nbytes = _lib.decode_workspace_bytes(B, B, 1, max(lens), hq_l, hkv_l, D, bs, dt, q.dtype, pt)
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
 
     def decode_only():
@@ -239,6 +243,13 @@ def build_step(cfg, rank, world, lens, device, seed=0):
                           status=pool.status)
 
     def step():
+        if gather is not None:
+            # fused append + decode, then reduce with the all-gather fused in
+            _lib.decode_step_gather(q, pool.k[0], pool.v[0], kn, vn, pool.tables, offs, ctx, gather,
+                                    max_queries_per_seq=1, max_ctx_len=max(lens),
+                                    score_scale=cfg.score_scale, seq_rows=rows, partition_tokens=pt,
+                                    workspace=ws, status=pool.status)
+            return
         # append each sequence's new token at position ctx-1 and attend (fused)
         _lib.decode_step(out, q, pool.k[0], pool.v[0], kn, vn, pool.tables, offs, ctx,
                          max_queries_per_seq=1, max_ctx_len=max(lens), score_scale=cfg.score_scale,
@@ -263,10 +274,16 @@ def run_b200(args):
         lens = (lens * (args.batch // len(lens) + 1))[:args.batch]
     B = len(lens)
     total_kv = kv_bytes(lens, cfg.num_kv_heads, cfg.head_dim, cfg.dtype)
-    st = build_step(cfg, rank, world, lens, device)
+    peer = None
+    if world > 1 and args.gather == "peer":
+        from cloverinfer_b200.head_groups import kv_head_shards
+        from cloverinfer_b200.sharded import HeadShardGroup, PeerGather
+        lo, hi = kv_head_shards(cfg.num_kv_heads, world)[rank]
+        peer = PeerGather(HeadShardGroup(), B, cfg.num_q_heads, cfg.head_dim, torch.float32, device)
+    st = build_step(cfg, rank, world, lens, device, gather=peer)
     local_kv = kv_bytes(lens, st["hkv_local"], cfg.head_dim, cfg.dtype)
     gather = None
-    if world > 1:
+    if world > 1 and peer is None:
         import torch.distributed as dist
         recv = torch.empty((world, B, st["hq_local"], cfg.head_dim), dtype=st["out"].dtype, device=device)
 
@@ -276,6 +293,7 @@ def run_b200(args):
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
     launches_per_step = 1 + (1 if st["workspace_bytes"] > 0 else 0)
+    gather_kind = "none" if world == 1 else ("fused-peer-stores" if peer is not None else "nccl")
 
     def full_step():
         st["step"]()
@@ -360,7 +378,8 @@ def run_b200(args):
                    "num_q_heads": cfg.num_q_heads, "num_kv_heads": cfg.num_kv_heads,
                    "head_dim": cfg.head_dim, "block_size": cfg.block_size,
                    "partition_tokens": st["partition_tokens"],
-                   "parallelism": f"kv-head-shard{world}", "cuda_graph": used_graph,
+                   "parallelism": f"kv-head-shard{world}", "gather": gather_kind,
+                   "cuda_graph": used_graph,
                    "l2": "inputs > L2 (KV %.0f MB per GPU)" % (local_kv / 1e6)},
         "steps_per_s": round(1e3 / ms, 2),
         "tokens_per_s": round(B * 1e3 / ms, 2),
@@ -381,6 +400,8 @@ def run_b200(args):
                                           "context; repeat_kv-expanded KV as upstream" % B}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if peer is not None:
+        peer.close()
     if world > 1:
         import torch.distributed as dist
         torch.cuda.synchronize(device)
@@ -456,6 +477,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="N>1 output all-gather: fused NVLink peer stores or NCCL")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

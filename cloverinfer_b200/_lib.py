@@ -53,6 +53,16 @@ SIGNATURES = {
     "clover_b200_decode_step": (ctypes.c_int, [
         _P, _I64, _P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _P, _I64, _P, _I32, _P, _P, _P,
         _I32, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _I64, _P, _P]),
+    "clover_b200_ipc_alloc": (ctypes.c_int, [_I64, _P, _P]),
+    "clover_b200_ipc_open": (ctypes.c_int, [_P, _P]),
+    "clover_b200_ipc_close": (ctypes.c_int, [_P]),
+    "clover_b200_ipc_free": (ctypes.c_int, [_P]),
+    "clover_b200_gather_sync_bytes": (ctypes.c_int64, []),
+    "clover_b200_decode_gather_workspace_bytes": (ctypes.c_int64, [_I32] * 11),
+    "clover_b200_decode_step_gather": (ctypes.c_int, [
+        _P, _I64, _P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _P, _I64, _P, _I32, _P, _P, _P,
+        _I32, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _P, _I32, _I32, _I64, _P, _I64,
+        _P, _P]),
     "clover_b200_paged_decode_noalloc": (ctypes.c_int, [
         _P, _I64, _P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _I32, _P, _P, _P,
         _I32, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _P]),
@@ -255,3 +265,74 @@ def decode_step(out, q, k_cache, v_cache, k_new, v_new, block_tables, query_star
         _stream(q.device))
     _check(rc, "clover_b200_decode_step")
 
+
+# ---------------------------------------------------------------- peer memory / fused gather
+IPC_HANDLE_BYTES = 64
+
+
+def ipc_alloc(nbytes: int):
+    """(device pointer, 64-byte IPC handle) of a zeroed cudaMalloc buffer."""
+    ptr = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    _check(lib().clover_b200_ipc_alloc(nbytes, ctypes.byref(ptr), h), "clover_b200_ipc_alloc")
+    return int(ptr.value), bytes(h.raw)
+
+
+def ipc_open(handle: bytes) -> int:
+    ptr = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES)
+    _check(lib().clover_b200_ipc_open(h, ctypes.byref(ptr)), "clover_b200_ipc_open")
+    return int(ptr.value)
+
+
+def ipc_close(ptr: int) -> None:
+    _check(lib().clover_b200_ipc_close(ptr), "clover_b200_ipc_close")
+
+
+def ipc_free(ptr: int) -> None:
+    _check(lib().clover_b200_ipc_free(ptr), "clover_b200_ipc_free")
+
+
+def gather_sync_bytes() -> int:
+    return int(lib().clover_b200_gather_sync_bytes())
+
+
+def decode_gather_workspace_bytes(n_seqs, n_rows, max_queries_per_seq, max_ctx_len, num_q_heads,
+                                  num_kv_heads, head_dim, block_size, kv_dtype, q_dtype,
+                                  partition_tokens=0) -> int:
+    nb = int(lib().clover_b200_decode_gather_workspace_bytes(
+        n_seqs, n_rows, max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads, head_dim,
+        block_size, dtype_code(kv_dtype), dtype_code(q_dtype), partition_tokens))
+    if nb < 0:
+        raise CloverB200Error(lib().clover_b200_last_error().decode(errors="replace"))
+    return nb
+
+
+def decode_step_gather(q, k_cache, v_cache, k_new, v_new, block_tables, query_start_loc, ctx_lens,
+                       gather, *, max_queries_per_seq, max_ctx_len, score_scale, seq_rows=None,
+                       partition_tokens=0, workspace=None, status=None):
+    """decode_step whose output, all-gathered over every rank of ``gather`` (a
+    PeerGather), lands in ``gather.out[:rows]`` ([rows, Hq_total, D])."""
+    _require_cuda(q, k_cache, v_cache, k_new, v_new, block_tables, query_start_loc, ctx_lens,
+                  seq_rows, workspace, status)
+    nb, bs, hkv, d = k_cache.shape
+    rows, hq, dq = q.shape
+    if dq != d or q.stride(2) != 1 or q.stride(1) != d:
+        raise ValueError("decode_step_gather: q must be [rows, Hq_local, D] with contiguous rows")
+    if q.dtype != gather.out.dtype or rows > gather.out.shape[0] or hq * gather.world != gather.out.shape[1]:
+        raise ValueError("decode_step_gather: q does not fit the gather buffers")
+    if k_new is not None and (k_new.shape != (rows, hkv, d) or v_new.shape != k_new.shape
+                              or k_new.dtype != k_cache.dtype):
+        raise ValueError("decode_step_gather: new K/V must be [rows, Hkv_local, D] in the cache dtype")
+    n_seqs = query_start_loc.numel() - 1
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    out = gather.out
+    rc = lib().clover_b200_decode_step_gather(
+        _ptr(out), out.stride(0), _ptr(q), q.stride(0), dtype_code(q.dtype), _ptr(k_cache),
+        _ptr(v_cache), dtype_code(k_cache.dtype), nb, bs, _ptr(k_new), _ptr(v_new),
+        0 if k_new is None else k_new.stride(0), _ptr(block_tables), block_tables.stride(0),
+        _ptr(seq_rows), _ptr(query_start_loc), _ptr(ctx_lens), n_seqs, rows,
+        max_queries_per_seq, max_ctx_len, hq, hkv, d, float(score_scale), partition_tokens,
+        gather.peer_recv_d.data_ptr(), gather.sync.data_ptr(), gather.world, gather.rank,
+        gather.half_words, _ptr(workspace), ws_bytes, _ptr(status), _stream(q.device))
+    _check(rc, "clover_b200_decode_step_gather")

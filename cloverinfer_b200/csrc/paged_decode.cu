@@ -30,6 +30,7 @@
 // SIMT path (fp32 cache or other shapes): same decomposition and workspace
 // format with CUDA-core dot products.
 #include <math.h>
+#include <cmath>
 #include <mutex>
 
 #include <cudaTypedefs.h>
@@ -91,6 +92,28 @@ struct DecodeArgs {
   const void* v_new;
   int64_t new_stride;
   int32_t kv_esz;
+  // Gathered output (decode_step_gather): every row goes through the split-K
+  // workspace, even a single-partition one, and the reduce writes the output.
+  int32_t force_split;
+};
+
+// Fused output all-gather over peer memory, LL style: every value travels as
+// one 8-byte word (epoch << 32 | fp32 bits) written with a single 64-bit
+// store, so a reader that sees the current epoch in a word also sees its
+// value — no fences and no global barrier.  Words live in each rank's receive
+// buffer, [2 parities][rows, total_q_heads, D] (parity = epoch & 1).  The
+// local sync words: kSyncDone counts finished reduce CTAs of this launch;
+// kSyncEpoch is the number of completed calls.
+constexpr int kSyncDone = 0;
+constexpr int kSyncEpoch = 1;
+constexpr int kSyncInts = 64;
+
+struct GatherArgs {
+  uint64_t* const* peer_ll;  // [n_ranks] receive buffers (own one at [rank])
+  int32_t* sync;             // this rank's sync words
+  int32_t n_ranks, rank, q_head_offset, total_q_heads;
+  int64_t ll_half_words;     // words per parity half (>= rows * total_q_heads * D)
+  int32_t units;             // rows * local heads * 32-dim chunks
 };
 
 struct ColInfo {
@@ -136,6 +159,7 @@ struct CtaWork {
 
 // Columns whose context is empty attend to nothing: their output is zero.
 __device__ __forceinline__ void zero_empty_columns(const DecodeArgs& a, const CtaWork& w, int D) {
+  if (a.force_split) return;  // the gather reduce writes empty rows
   for (int idx = threadIdx.x; idx < a.cols_per_cta * D; idx += blockDim.x) {
     const int col = idx / D;
     const ColInfo ci = col_info(a, w.row0, w.nq, w.kvh, w.chunk * a.cols_per_cta + col);
@@ -251,7 +275,8 @@ __device__ __forceinline__ void merge_store_rt(const DecodeArgs& a, const CtaWor
     const ColInfo ci = col_info(a, w.row0, w.nq, w.kvh, w.chunk * a.cols_per_cta + col);
     if (!ci.valid) continue;
     if (ci.limit <= w.tok_begin) {
-      if (w.p == 0) store_out(a, (int64_t)ci.qrow * a.out_stride + (int64_t)ci.qhead * D + dim, 0.f);
+      if (w.p == 0 && !a.force_split)
+        store_out(a, (int64_t)ci.qrow * a.out_stride + (int64_t)ci.qhead * D + dim, 0.f);
       continue;
     }
     float M = -INFINITY;
@@ -268,7 +293,7 @@ __device__ __forceinline__ void merge_store_rt(const DecodeArgs& a, const CtaWor
     }
     const float o = L > 0.f ? O / L : 0.f;
     const int nparts = (ci.limit + a.part_tokens - 1) / a.part_tokens;
-    if (nparts == 1) {
+    if (nparts == 1 && !a.force_split) {
       store_out(a, (int64_t)ci.qrow * a.out_stride + (int64_t)ci.qhead * D + dim, o);
     } else {
       const int64_t base = ((int64_t)ci.qrow * a.num_q_heads + ci.qhead) * a.max_parts + w.p;
@@ -673,18 +698,19 @@ paged_decode_simt_kernel(const DecodeArgs a, int D) {
 }
 
 // ------------------------------------------------------------------ split-K reduce
-// One CTA (4 warps) per (query row, head).  The partitions' log-sum-exp
-// weights are computed once into shared memory; warp w sums partitions
-// w, w+4, ... with lanes covering EPL consecutive dims (float4 for D = 128);
-// the four warp sums are combined in shared memory.
+// Grid (query row, head, 32-dim chunk), 4 warps.  The partitions'
+// log-sum-exp weights are computed once per CTA into shared memory; warp w
+// sums partitions w, w+4, ... for the chunk's 32 dims (lane = dim, coalesced
+// 128-byte loads, 8 partitions in flight per warp); the four warp sums are
+// combined in shared memory.
 constexpr int kReduceWarps = 4;
 constexpr int kReduceMaxParts = 1024;
+constexpr int kReduceDims = 32;
 
-template <int EPL>
 __global__ void __launch_bounds__(kReduceWarps * 32)
 splitk_reduce_kernel(const DecodeArgs a, int D) {
   __shared__ float s_w[kReduceMaxParts];
-  __shared__ float s_red[kReduceWarps][32 * EPL];
+  __shared__ float s_red[kReduceWarps][kReduceDims];
   __shared__ float s_wmax[kReduceWarps], s_wsum[kReduceWarps];
   const int r = blockIdx.x;
   const int h = blockIdx.y;
@@ -695,9 +721,8 @@ splitk_reduce_kernel(const DecodeArgs a, int D) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t base = ((int64_t)r * a.num_q_heads + h) * a.max_parts;
   const float* lse = a.part_lse + base;
-  // max and weights
   float M = -INFINITY;
-  for (int p = threadIdx.x; p < npp; p += blockDim.x) M = fmaxf(M, lse[p]);
+  for (int p = threadIdx.x; p < npp; p += blockDim.x) M = fmaxf(M, __ldcg(lse + p));
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
   if (lane == 0) s_wmax[warp] = M;
@@ -705,7 +730,7 @@ splitk_reduce_kernel(const DecodeArgs a, int D) {
   M = fmaxf(fmaxf(s_wmax[0], s_wmax[1]), fmaxf(s_wmax[2], s_wmax[3]));
   float L = 0.f;
   for (int p = threadIdx.x; p < npp; p += blockDim.x) {
-    const float wt = M == -INFINITY ? 0.f : fast_exp2(lse[p] - M);
+    const float wt = M == -INFINITY ? 0.f : fast_exp2(__ldcg(lse + p) - M);
     s_w[p] = wt;
     L += wt;
   }
@@ -714,39 +739,136 @@ splitk_reduce_kernel(const DecodeArgs a, int D) {
   if (lane == 0) s_wsum[warp] = L;
   __syncthreads();
   L = (s_wsum[0] + s_wsum[1]) + (s_wsum[2] + s_wsum[3]);
-  // weighted sum of the partial outputs
-  const int d0 = lane * EPL;
-  float o[EPL];
+  const int dim = blockIdx.z * kReduceDims + lane;
+  float o = 0.f;
+  if (dim < D) {
+    const float* po = a.part_out + base * D + dim;
+#pragma unroll 8
+    for (int p = warp; p < npp; p += kReduceWarps) o = fmaf(s_w[p], __ldcg(po + (int64_t)p * D), o);
+  }
+  s_red[warp][lane] = o;
+  __syncthreads();
+  if (warp == 0 && dim < D) {
+    const float v = (s_red[0][lane] + s_red[1][lane]) + (s_red[2][lane] + s_red[3][lane]);
+    store_out(a, (int64_t)r * a.out_stride + (int64_t)h * D + dim, L > 0.f ? v / L : 0.f);
+  }
+}
+
+// Split-K reduce with the output all-gather fused in.  A unit is (query row,
+// local head, 32-dim chunk).  Phase 1: every CTA reduces its units (1 or more
+// partitions; 0 -> zeros) and stores each value, tagged with the epoch, into
+// EVERY rank's receive buffer over NVLink.  Phase 2: every CTA waits (bounded)
+// until its units' words from every rank carry the epoch and writes them to
+// the output [rows, total_q_heads, D] in place.  The grid never exceeds the
+// co-resident CTA count and each CTA sends before it waits, so no CTA can wait
+// on a CTA that has not started.
+constexpr int kGatherCtasPerSm = 4;
+
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(kReduceWarps * 32)
+reduce_gather_kernel(const DecodeArgs a, const GatherArgs g, int D) {
+  __shared__ float s_w[kReduceMaxParts];
+  __shared__ float s_red[kReduceWarps][kReduceDims];
+  __shared__ float s_wmax[kReduceWarps], s_wsum[kReduceWarps];
+  __shared__ int s_last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int epoch = *(volatile int32_t*)(g.sync + kSyncEpoch) + 1;
+  const int64_t half = (int64_t)(epoch & 1) * g.ll_half_words;
+  const int dchunks = (D + kReduceDims - 1) / kReduceDims;
+  const int heads = a.num_q_heads;
+
+  // ---- phase 1: reduce and send
+  for (int u = blockIdx.x; u < g.units; u += gridDim.x) {
+    const int dc = u % dchunks;
+    const int h = (u / dchunks) % heads;
+    const int r = u / (dchunks * heads);
+    const int lim = __ldg(a.ctx + r);
+    const int np = lim > 0 ? (lim + a.part_tokens - 1) / a.part_tokens : 0;
+    const int npp = min(min(np, a.max_parts), kReduceMaxParts);
+    const int64_t base = ((int64_t)r * heads + h) * a.max_parts;
+    const float* lse = a.part_lse + base;
+    float M = -INFINITY;
+    for (int p = threadIdx.x; p < npp; p += blockDim.x) M = fmaxf(M, __ldcg(lse + p));
 #pragma unroll
-  for (int e = 0; e < EPL; ++e) o[e] = 0.f;
-  const float* po = a.part_out + base * D + d0;
-  if (EPL == 4 && D == 128) {
-#pragma unroll 4
-    for (int p = warp; p < npp; p += kReduceWarps) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(po + (int64_t)p * D));
-      const float wt = s_w[p];
-      o[0] = fmaf(wt, v.x, o[0]);
-      o[1] = fmaf(wt, v.y, o[1]);
-      o[2] = fmaf(wt, v.z, o[2]);
-      o[3] = fmaf(wt, v.w, o[3]);
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    if (lane == 0) s_wmax[warp] = M;
+    __syncthreads();
+    M = fmaxf(fmaxf(s_wmax[0], s_wmax[1]), fmaxf(s_wmax[2], s_wmax[3]));
+    float L = 0.f;
+    for (int p = threadIdx.x; p < npp; p += blockDim.x) {
+      const float wt = M == -INFINITY ? 0.f : fast_exp2(__ldcg(lse + p) - M);
+      s_w[p] = wt;
+      L += wt;
     }
-  } else {
-#pragma unroll 4
-    for (int p = warp; p < npp; p += kReduceWarps) {
-      const float wt = s_w[p];
 #pragma unroll
-      for (int e = 0; e < EPL; ++e)
-        if (d0 + e < D) o[e] = fmaf(wt, __ldcg(po + (int64_t)p * D + e), o[e]);
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    if (lane == 0) s_wsum[warp] = L;
+    __syncthreads();
+    L = (s_wsum[0] + s_wsum[1]) + (s_wsum[2] + s_wsum[3]);
+    const int dim = dc * kReduceDims + lane;
+    float o = 0.f;
+    if (dim < D) {
+      const float* po = a.part_out + base * D + dim;
+#pragma unroll 8
+      for (int p = warp; p < npp; p += kReduceWarps) o = fmaf(s_w[p], __ldcg(po + (int64_t)p * D), o);
+    }
+    s_red[warp][lane] = o;
+    __syncthreads();
+    if (warp == 0 && dim < D) {
+      const float v =
+          L > 0.f ? ((s_red[0][lane] + s_red[1][lane]) + (s_red[2][lane] + s_red[3][lane])) / L : 0.f;
+      const uint64_t word = ((uint64_t)(uint32_t)epoch << 32) | (uint64_t)__float_as_uint(v);
+      const int64_t idx = half + ((int64_t)r * g.total_q_heads + g.q_head_offset + h) * D + dim;
+      for (int rr = 0; rr < g.n_ranks; ++rr) st_relaxed_sys_u64(g.peer_ll[rr] + idx, word);
+    }
+    __syncthreads();  // shared buffers are reused by the next unit
+  }
+
+  // ---- phase 2: receive every rank's words for this CTA's units
+  bool timed_out = false;
+  const uint64_t t0 = global_timer_ns();
+  for (int u = blockIdx.x; u < g.units; u += gridDim.x) {
+    const int dc = u % dchunks;
+    const int h = (u / dchunks) % heads;
+    const int r = u / (dchunks * heads);
+    const int dim = dc * kReduceDims + lane;
+    if (dim >= D) continue;
+    for (int rr = warp; rr < g.n_ranks; rr += kReduceWarps) {
+      const int head = rr * heads + h;  // ranks hold equal, contiguous head ranges
+      const uint64_t* src = g.peer_ll[g.rank] + half + ((int64_t)r * g.total_q_heads + head) * D + dim;
+      uint64_t w = ld_relaxed_sys_u64(src);
+      while ((uint32_t)(w >> 32) != (uint32_t)epoch && !timed_out) {
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+          timed_out = true;
+          break;
+        }
+        w = ld_relaxed_sys_u64(src);
+      }
+      const float v = __uint_as_float((uint32_t)w);
+      const int64_t oidx = (int64_t)r * a.out_stride + (int64_t)head * D + dim;
+      store_out(a, oidx, timed_out ? 0.f : v);
     }
   }
-#pragma unroll
-  for (int e = 0; e < EPL; ++e) s_red[warp][d0 + e] = o[e];
+  if (timed_out) raise_status(a.status, CLOVER_B200_DEV_TIMEOUT);
+
+  // ---- the last CTA advances this rank's epoch
   __syncthreads();
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  const int64_t obase = (int64_t)r * a.out_stride + (int64_t)h * D;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    const float v = (s_red[0][d] + s_red[1][d]) + (s_red[2][d] + s_red[3][d]);
-    store_out(a, obase + d, v * inv);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    s_last = atomicAdd(g.sync + kSyncDone, 1) == (int)gridDim.x - 1;
+  }
+  __syncthreads();
+  if (s_last && threadIdx.x == 0) {
+    g.sync[kSyncDone] = 0;
+    *(volatile int32_t*)(g.sync + kSyncEpoch) = epoch;
   }
 }
 
@@ -814,19 +936,37 @@ static int MmaGeomBps(int BS) {
 static int max_mma_partition(int BS) { return 32 * kMmaWarps * MmaGeomBps(BS) * BS; }
 
 static int choose_partition(int max_ctx, int BS, int rows_x_kvh, bool mma) {
-  // 512-token partitions by default (flash-decoding split); shorter contexts
-  // with few (row, head) units split finer so the grid still covers the GPU.
-  int pt = 512;
-  const int min_pt = BS * (mma ? kMmaWarps * MmaGeomBps(BS) : kNumWarps);
-  // two waves of the tensor-core kernel's resident CTAs (148 SMs)
-  const int64_t want = 2 * 148 * (mma ? CLOVER_MMA_MIN_CTAS : 4);
-  while (pt > min_pt && (int64_t)rows_x_kvh * ((max_ctx + pt - 1) / pt) < want &&
-         (max_ctx + pt / 2 - 1) / (pt / 2) <= kReduceMaxParts)
-    pt /= 2;
-  if (pt < min_pt) pt = min_pt;
-  while ((max_ctx + pt - 1) / pt > kReduceMaxParts) pt *= 2;  // very long contexts
-  pt = (pt + BS - 1) / BS * BS;
-  if (mma && pt > max_mma_partition(BS)) pt = max_mma_partition(BS);
+  if (max_ctx <= 0) return BS * 4;
+  if (!mma) {
+    // SIMT path: 512-token partitions, finer when there are few (row, head) units
+    int pt = 512;
+    while (pt > 64 && (int64_t)rows_x_kvh * ((max_ctx + pt - 1) / pt) < 2 * 148 * 4) pt /= 2;
+    while ((max_ctx + pt - 1) / pt > kReduceMaxParts) pt *= 2;
+    return (pt + BS - 1) / BS * BS;
+  }
+  // Tensor-core path: the longest partition (fewest partials) whose CTA count
+  // fills the resident CTA slots in near-whole waves (>= 90 % of the last
+  // wave busy); contexts are assumed as long as the longest one.
+  const int64_t slots = 148LL * CLOVER_MMA_MIN_CTAS;
+  const int hi = max_mma_partition(BS) < 1024 ? max_mma_partition(BS) : 1024;
+  const int lo = BS * kMmaWarps * MmaGeomBps(BS);
+  int best = -1;
+  double best_eff = 0.0;
+  for (int pt = hi; pt >= lo; pt -= BS) {
+    const int64_t parts = (max_ctx + pt - 1) / pt;
+    if (parts > kReduceMaxParts) break;
+    const int64_t ctas = (int64_t)rows_x_kvh * parts;
+    const double waves = (double)ctas / (double)slots;
+    const double eff = waves / std::ceil(waves);
+    if (eff >= 0.9) return pt;
+    if (eff > best_eff) {
+      best_eff = eff;
+      best = pt;
+    }
+  }
+  if (best > 0) return best;
+  int pt = lo;
+  while ((max_ctx + pt - 1) / pt > kReduceMaxParts) pt *= 2;
   return pt;
 }
 
@@ -894,9 +1034,13 @@ static int launch_simt(int D, int nc, const DecodeArgs& a, dim3 grid, cudaStream
 
 static int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
-static int64_t workspace_bytes(int64_t rows, int64_t hq, int64_t D, int64_t parts) {
-  if (parts <= 1) return 0;
+static int64_t split_workspace_bytes(int64_t rows, int64_t hq, int64_t D, int64_t parts) {
+  if (parts < 1) parts = 1;
   return align256(rows * hq * parts * D * 4) + align256(rows * hq * parts * 4);
+}
+
+static int64_t workspace_bytes(int64_t rows, int64_t hq, int64_t D, int64_t parts) {
+  return parts <= 1 ? 0 : split_workspace_bytes(rows, hq, D, parts);
 }
 
 struct DecodePlan {
@@ -987,7 +1131,7 @@ static int decode_impl(
     int32_t n_seqs, int32_t n_query_rows, int32_t max_queries_per_seq, int32_t max_ctx_len,
     int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, float score_scale,
     int32_t partition_tokens, void* workspace, int64_t workspace_bytes_, int32_t* dev_status,
-    void* stream) {
+    void* stream, const GatherArgs* gather) {
   if (table_stride <= 0 || num_blocks <= 0)
     return set_error(CLOVER_B200_ERR_INVALID_ARG, "paged_decode: bad sizes");
   DecodePlan pl;
@@ -995,9 +1139,11 @@ static int decode_impl(
                      num_kv_heads, head_dim, block_size, kv_dtype, q_dtype, partition_tokens, &pl);
   if (rc) return rc;
   if (n_seqs == 0 || n_query_rows == 0) return CLOVER_B200_OK;
-  if (!out || !q || !k_cache || !v_cache || !block_tables || !query_start_loc || !ctx_lens)
+  if ((!out && !gather) || !q || !k_cache || !v_cache || !block_tables || !query_start_loc ||
+      !ctx_lens)
     return set_error(CLOVER_B200_ERR_INVALID_ARG, "paged_decode: null pointer");
-  if (q_row_stride < (int64_t)num_q_heads * head_dim || out_row_stride < (int64_t)num_q_heads * head_dim)
+  if (q_row_stride < (int64_t)num_q_heads * head_dim ||
+      (!gather && out_row_stride < (int64_t)num_q_heads * head_dim))
     return set_error(CLOVER_B200_ERR_INVALID_ARG, "paged_decode: row stride < heads*head_dim");
   if (n_seqs > 65535 || (int64_t)num_kv_heads * pl.col_chunks > 65535)
     return set_error(CLOVER_B200_ERR_UNSUPPORTED, "paged_decode: grid too large");
@@ -1007,7 +1153,8 @@ static int decode_impl(
     if (num_blocks * (int64_t)block_size > INT32_MAX)
       return set_error(CLOVER_B200_ERR_UNSUPPORTED, "paged_decode: cache exceeds 2^31 slots");
   }
-  const int64_t need = pl.workspace_bytes;
+  const int64_t need = gather ? split_workspace_bytes(n_query_rows, num_q_heads, head_dim, pl.max_parts)
+                              : pl.workspace_bytes;
   if (need > 0 && (workspace == nullptr || workspace_bytes_ < need))
     return set_error(CLOVER_B200_ERR_WORKSPACE, "paged_decode: workspace needs %lld bytes",
                      (long long)need);
@@ -1051,6 +1198,7 @@ static int decode_impl(
   a.v_new = nullptr;
   a.new_stride = new_token_stride;
   a.kv_esz = kv_dtype == CLOVER_B200_F32 ? 4 : 2;
+  a.force_split = gather != nullptr;
 
   cudaStream_t s = (cudaStream_t)stream;
   if (k_new != nullptr) {
@@ -1098,19 +1246,22 @@ static int decode_impl(
     }
   }
   if (rc) return rc;
+  if (gather != nullptr) {
+    GatherArgs g = *gather;
+    g.units = n_query_rows * num_q_heads * ((head_dim + kReduceDims - 1) / kReduceDims);
+    int sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int grid = g.units < sms * kGatherCtasPerSm ? g.units : sms * kGatherCtasPerSm;
+    reduce_gather_kernel<<<grid, kReduceWarps * 32, 0, s>>>(a, g, head_dim);
+    return check_cuda(cudaGetLastError(), "reduce_gather launch");
+  }
   if (max_parts > 1) {
     // Rows with several partitions are combined here; single-partition rows
     // were written by the decode kernel and return at once.
-    const dim3 rgrid(n_query_rows, num_q_heads);
-    const int rt = kReduceWarps * 32;
-    if (head_dim <= 32)
-      splitk_reduce_kernel<1><<<rgrid, rt, 0, s>>>(a, head_dim);
-    else if (head_dim <= 64)
-      splitk_reduce_kernel<2><<<rgrid, rt, 0, s>>>(a, head_dim);
-    else if (head_dim <= 128)
-      splitk_reduce_kernel<4><<<rgrid, rt, 0, s>>>(a, head_dim);
-    else
-      splitk_reduce_kernel<8><<<rgrid, rt, 0, s>>>(a, head_dim);
+    const dim3 rgrid(n_query_rows, num_q_heads, (head_dim + kReduceDims - 1) / kReduceDims);
+    splitk_reduce_kernel<<<rgrid, kReduceWarps * 32, 0, s>>>(a, head_dim);
     rc = check_cuda(cudaGetLastError(), "splitk_reduce launch");
   }
   return rc;
@@ -1129,7 +1280,8 @@ extern "C" int clover_b200_paged_decode(
                      num_blocks, block_size, nullptr, nullptr, 0, block_tables, table_stride,
                      seq_rows, query_start_loc, ctx_lens, n_seqs, n_query_rows,
                      max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads, head_dim,
-                     score_scale, partition_tokens, workspace, workspace_bytes_, dev_status, stream);
+                     score_scale, partition_tokens, workspace, workspace_bytes_, dev_status, stream,
+                     nullptr);
 }
 
 extern "C" int clover_b200_decode_step(
@@ -1147,5 +1299,51 @@ extern "C" int clover_b200_decode_step(
                      num_blocks, block_size, k_new, v_new, new_token_stride, block_tables,
                      table_stride, seq_rows, query_start_loc, ctx_lens, n_seqs, n_query_rows,
                      max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads, head_dim,
-                     score_scale, partition_tokens, workspace, workspace_bytes_, dev_status, stream);
+                     score_scale, partition_tokens, workspace, workspace_bytes_, dev_status, stream,
+                     nullptr);
+}
+
+extern "C" int64_t clover_b200_decode_gather_workspace_bytes(
+    int32_t n_seqs, int32_t n_query_rows, int32_t max_queries_per_seq, int32_t max_ctx_len,
+    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+    int32_t kv_dtype, int32_t q_dtype, int32_t partition_tokens) {
+  DecodePlan pl;
+  if (make_plan(n_seqs, n_query_rows, max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads,
+                head_dim, block_size, kv_dtype, q_dtype, partition_tokens, &pl) != CLOVER_B200_OK)
+    return -1;
+  return split_workspace_bytes(n_query_rows, num_q_heads, head_dim, pl.max_parts);
+}
+
+extern "C" int64_t clover_b200_gather_sync_bytes(void) { return (int64_t)kSyncInts * 4; }
+
+extern "C" int clover_b200_decode_step_gather(
+    void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride, int32_t q_dtype,
+    void* k_cache, void* v_cache, int32_t kv_dtype, int64_t num_blocks, int32_t block_size,
+    const void* k_new, const void* v_new, int64_t new_token_stride, const int32_t* block_tables,
+    int32_t table_stride, const int32_t* seq_rows, const int32_t* query_start_loc,
+    const int32_t* ctx_lens, int32_t n_seqs, int32_t n_query_rows, int32_t max_queries_per_seq,
+    int32_t max_ctx_len, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+    float score_scale, int32_t partition_tokens, void* const* peer_recv, int32_t* sync,
+    int32_t n_ranks, int32_t rank, int64_t recv_half_words, void* workspace,
+    int64_t workspace_bytes_, int32_t* dev_status, void* stream) {
+  const int64_t total_q_heads = (int64_t)num_q_heads * n_ranks;
+  if (!out || !peer_recv || !sync || n_ranks <= 0 || rank < 0 || rank >= n_ranks ||
+      out_row_stride < total_q_heads * head_dim ||
+      recv_half_words < (int64_t)n_query_rows * total_q_heads * head_dim)
+    return set_error(CLOVER_B200_ERR_INVALID_ARG, "decode_step_gather: bad gather arguments");
+  GatherArgs g;
+  g.peer_ll = reinterpret_cast<uint64_t* const*>(peer_recv);
+  g.sync = sync;
+  g.n_ranks = n_ranks;
+  g.rank = rank;
+  g.q_head_offset = rank * num_q_heads;
+  g.total_q_heads = (int32_t)total_q_heads;
+  g.ll_half_words = recv_half_words;
+  g.units = 0;
+  return decode_impl(out, out_row_stride, q, q_row_stride, q_dtype, k_cache, v_cache, kv_dtype,
+                     num_blocks, block_size, k_new, v_new, new_token_stride, block_tables,
+                     table_stride, seq_rows, query_start_loc, ctx_lens, n_seqs, n_query_rows,
+                     max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads, head_dim,
+                     score_scale, partition_tokens, workspace, workspace_bytes_, dev_status, stream,
+                     &g);
 }

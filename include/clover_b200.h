@@ -220,6 +220,65 @@ CLOVER_B200_API int clover_b200_decode_step(void* out, int64_t out_row_stride,
                              int32_t* dev_status, void* stream);
 
 /*
+ * Fused output all-gather for KV-head sharding (one process per GPU of a node).
+ *
+ * Rank r of n_ranks owns the contiguous query heads [r * num_q_heads,
+ * (r + 1) * num_q_heads) of total = n_ranks * num_q_heads (equal shards).
+ * decode_step_gather runs the fused append + decode of clover_b200_decode_step
+ * and then a split-K reduce that sends every output value, tagged with the
+ * call's epoch in one 8-byte word, straight into EVERY rank's receive buffer
+ * over NVLink (plain peer stores, no multicast), waits (bounded) for the
+ * words of its rows from every rank and writes out[rows, total, head_dim]
+ * (row stride out_row_stride, q dtype): the all-gathered output, on every
+ * rank, without a fence, a global barrier or a second kernel.
+ *
+ *   peer_recv[n_ranks]  device array of each rank's receive buffer (mapped here
+ *                       with clover_b200_ipc_open; this rank's own at [rank]):
+ *                       2 * recv_half_words uint64 words, zeroed at allocation.
+ *   sync                this rank's clover_b200_gather_sync_bytes() of
+ *                       zeroed device memory (call count, CTA count).
+ *
+ * Every rank must make the same sequence of calls with the same sizes.  A
+ * rank that does not arrive within 1 s makes the others finish with
+ * CLOVER_B200_DEV_TIMEOUT set (missing values read as 0).  Workspace:
+ * clover_b200_decode_gather_workspace_bytes(...).  k_new/v_new may be NULL
+ * (attend only).  Replaces: the per-layer hand-off of attention contexts to the
+ * dense node (src/core/scheduler.py:1058-1059) for heads split across GPUs by
+ * the head-grouping policy (src/core/attention_backend.py:429-438).
+ */
+#define CLOVER_B200_IPC_HANDLE_BYTES 64
+
+/* cudaMalloc'd, zeroed device buffer plus its IPC handle (64 bytes). */
+CLOVER_B200_API int clover_b200_ipc_alloc(int64_t bytes, void** dev_ptr, void* handle);
+/* Map a peer process's buffer from its handle (enables peer access). */
+CLOVER_B200_API int clover_b200_ipc_open(const void* handle, void** dev_ptr);
+/* Unmap a buffer opened with clover_b200_ipc_open. */
+CLOVER_B200_API int clover_b200_ipc_close(void* dev_ptr);
+/* Free a buffer from clover_b200_ipc_alloc (after every peer closed it). */
+CLOVER_B200_API int clover_b200_ipc_free(void* dev_ptr);
+CLOVER_B200_API int64_t clover_b200_gather_sync_bytes(void);
+CLOVER_B200_API int64_t clover_b200_decode_gather_workspace_bytes(int32_t n_seqs,
+                                           int32_t n_query_rows, int32_t max_queries_per_seq,
+                                           int32_t max_ctx_len, int32_t num_q_heads,
+                                           int32_t num_kv_heads, int32_t head_dim,
+                                           int32_t block_size, int32_t kv_dtype, int32_t q_dtype,
+                                           int32_t partition_tokens);
+CLOVER_B200_API int clover_b200_decode_step_gather(void* out, int64_t out_row_stride,
+                             const void* q, int64_t q_row_stride, int32_t q_dtype,
+                             void* k_cache, void* v_cache, int32_t kv_dtype,
+                             int64_t num_blocks, int32_t block_size,
+                             const void* k_new, const void* v_new, int64_t new_token_stride,
+                             const int32_t* block_tables, int32_t table_stride,
+                             const int32_t* seq_rows, const int32_t* query_start_loc,
+                             const int32_t* ctx_lens, int32_t n_seqs, int32_t n_query_rows,
+                             int32_t max_queries_per_seq, int32_t max_ctx_len,
+                             int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                             float score_scale, int32_t partition_tokens,
+                             void* const* peer_recv, int32_t* sync, int32_t n_ranks, int32_t rank,
+                             int64_t recv_half_words, void* workspace, int64_t workspace_bytes,
+                             int32_t* dev_status, void* stream);
+
+/*
  * Allocation-free paged decode.  No counterpart in the upstream project: it
  * exists for callers that cannot call cudaMalloc (a serving engine that owns
  * all of HBM through its own pool, or a foreign-function host without a CUDA
