@@ -420,7 +420,8 @@ def run_e2e(cfg, lens, rank, world, device, args):
                               block_size=cfg.block_size, num_kv_heads=cfg.num_kv_heads, kv_dtype=dt,
                               device=device, max_seqs=B, shard=shard, shuffle_seed=77,
                               partition_tokens=cfg.partition_tokens if world == 1 else 0,
-                              max_seq_len=max(lens) + 4096)
+                              max_seq_len=max(lens) + 4096, gather=args.gather,
+                              max_rows_per_call=B)
     g = torch.Generator(device=device).manual_seed(99)
     lo, hi = (0, cfg.num_kv_heads) if shard is None else shard.kv_range(cfg.num_kv_heads)
     for i, n in enumerate(lens):
@@ -460,11 +461,13 @@ def run_e2e(cfg, lens, rank, world, device, args):
                    for s in range(args.steps)) / args.steps
     for i in range(B):
         be.free_request(f"r{i}")
+    be.close()
     del be
     torch.cuda.empty_cache()
     return {"value": round(attended / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 5),
-            "api": "B200AttentionBackend.decode_layer_batch (per-item host tensors)"}
+            "api": "B200AttentionBackend.decode_layer_batch (per-item host tensors)",
+            "gather": "none" if world == 1 else args.gather}
 
 
 def main():

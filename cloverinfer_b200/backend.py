@@ -60,6 +60,28 @@ class _Stats:
     kv_bytes_read: int = 0
 
 
+class _Staging:
+    """Reused pinned host + device byte buffers for the host-tensor path: one
+    H2D copy carries a batch's queries, new K/V and index metadata.  Safe to
+    reuse because that path synchronises before returning."""
+
+    def __init__(self, device: torch.device) -> None:
+        self.device = device
+        self.host: Optional[torch.Tensor] = None
+        self.dev: Optional[torch.Tensor] = None
+
+    def get(self, nbytes: int):
+        if self.host is None or self.host.numel() < nbytes:
+            n = max(nbytes, 1 << 20, 2 * (0 if self.host is None else self.host.numel()))
+            self.host = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+            self.dev = torch.empty(n, dtype=torch.uint8, device=self.device)
+        return self.host, self.dev
+
+
+def _align(n: int) -> int:
+    return -(-n // 256) * 256
+
+
 def _default_device() -> torch.device:
     if not torch.cuda.is_available():
         raise RuntimeError("B200AttentionBackend requires a CUDA device (no CPU fallback)")
@@ -73,6 +95,7 @@ class B200AttentionBackend:
                  num_kv_heads: Optional[int] = None, kv_dtype: Optional[torch.dtype] = None,
                  device=None, kv_cache_fraction: float = 0.5, partition_tokens: int = 0,
                  shard=None, check_status: bool = True, shuffle_seed: Optional[int] = None,
+                 gather: str = "peer", max_rows_per_call: Optional[int] = None,
                  **_unused) -> None:
         self.device = torch.device(device) if device is not None else _default_device()
         if self.device.type != "cuda":
@@ -89,6 +112,11 @@ class B200AttentionBackend:
         self.shard = shard
         self.check_status = bool(check_status)
         self.shuffle_seed = shuffle_seed
+        if gather not in ("peer", "nccl"):
+            raise ValueError("gather must be 'peer' or 'nccl'")
+        self.gather_mode = gather
+        self.max_rows_per_call = int(max_rows_per_call or 4 * self.max_seqs)
+        self._peer = None
         self.pool: Optional[PagedKVPool] = None
         self.num_layers = 0
         self.num_kv_heads = 0  # total (all shards)
@@ -96,6 +124,10 @@ class B200AttentionBackend:
         self.kv_range = (0, 0)
         self._reqs: Dict[str, _Request] = {}
         self.stats = _Stats()
+        self._stage_in = _Staging(self.device)
+        self._stage_out: Optional[torch.Tensor] = None
+        self._status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self._kv_esz = 0
 
     # ------------------------------------------------------------ setup
     def _ensure_pool(self, num_layers: int, heads: int, head_dim: int, dtype: torch.dtype) -> None:
@@ -112,6 +144,7 @@ class B200AttentionBackend:
         if dt not in (torch.float32, torch.float16, torch.bfloat16):
             raise TypeError(f"unsupported KV dtype {dt}")
         self.num_layers, self.num_kv_heads, self.head_dim, self.kv_dtype = num_layers, hkv, head_dim, dt
+        self._kv_esz = torch.empty((), dtype=dt).element_size()
         if self.shard is not None:
             self.kv_range = self.shard.kv_range(hkv)
         else:
@@ -213,27 +246,63 @@ class B200AttentionBackend:
         for r in rids:
             if r not in self._reqs:
                 raise KeyError(f"Unknown request {r}")
-        qs = [it["query"] for it in items]
-        q_dtype = qs[0].dtype
-        on_host = not qs[0].is_cuda
         sq = lambda t: t.squeeze(0) if t.dim() == 3 else t  # noqa: E731
-        if on_host:
-            q = torch.stack([sq(t) for t in qs]).pin_memory().to(self.device, non_blocking=True)
-            k = torch.stack([sq(it["key"]) for it in items]).pin_memory()
-            v = torch.stack([sq(it["value"]) for it in items]).pin_memory()
-        else:
-            q = torch.stack([sq(t) for t in qs])
-            k = torch.stack([sq(it["key"]) for it in items])
-            v = torch.stack([sq(it["value"]) for it in items])
-        out = self.decode_batch(rids, layer, q, k, v, scale)
-        if on_host:
-            out = out.to("cpu")
+        qs = [sq(it["query"]) for it in items]
+        ks = [sq(it["key"]) for it in items]
+        vs = [sq(it["value"]) for it in items]
+        q_dtype = qs[0].dtype
+        uniform = (all(t.dtype == q_dtype and not t.is_cuda for t in qs)
+                   and all(t.dtype == ks[0].dtype and not t.is_cuda for t in ks + vs)
+                   and q_dtype in (torch.float32, torch.float16, torch.bfloat16))
+        if not uniform:  # device tensors (or mixed inputs): no staging, no host sync
+            out = self.decode_batch(rids, layer, torch.stack(qs), torch.stack(ks), torch.stack(vs), scale)
+            if not qs[0].is_cuda:
+                out = out.to("cpu")
+            if out.dtype != q_dtype:
+                out = out.to(q_dtype)
+            if self.check_status and not qs[0].is_cuda:
+                self.pool.check_status()
+            for n in range(len(items)):
+                results[base + n] = out[n:n + 1]
+            return
+        B = len(items)
+        n_new = [1] * B
+        reqs, rows, targets, offs, ctx_rows = self._plan(rids, layer, n_new, qs[0].shape)
+        # one pinned staging buffer -> one H2D copy: q | k | v | int32 metadata
+        qb = _align(B * qs[0].numel() * qs[0].element_size())
+        kb = _align(B * ks[0].numel() * ks[0].element_size())
+        meta = rows + offs + ctx_rows
+        mb = _align(4 * len(meta))
+        total = qb + 2 * kb + mb
+        host, dev = self._stage_in.get(total)
+        torch.stack(qs, out=host[0:B * qs[0].numel() * qs[0].element_size()].view(q_dtype).view(B, *qs[0].shape))
+        kbytes = B * ks[0].numel() * ks[0].element_size()
+        torch.stack(ks, out=host[qb:qb + kbytes].view(ks[0].dtype).view(B, *ks[0].shape))
+        torch.stack(vs, out=host[qb + kb:qb + kb + kbytes].view(ks[0].dtype).view(B, *ks[0].shape))
+        host[qb + 2 * kb:qb + 2 * kb + 4 * len(meta)].view(torch.int32).copy_(
+            torch.tensor(meta, dtype=torch.int32))
+        dev[:total].copy_(host[:total], non_blocking=True)
+        qd = dev[0:B * qs[0].numel() * qs[0].element_size()].view(q_dtype).view(B, *qs[0].shape)
+        kd = dev[qb:qb + kbytes].view(ks[0].dtype).view(B, *ks[0].shape)
+        vd = dev[qb + kb:qb + kb + kbytes].view(ks[0].dtype).view(B, *ks[0].shape)
+        md = dev[qb + 2 * kb:qb + 2 * kb + 4 * len(meta)].view(torch.int32)
+        out = self._launch(reqs, layer, n_new, targets, qd, kd, vd, md[0:B], md[B:2 * B + 1],
+                           md[2 * B + 1:], scale)
+        # output and status word back in one synchronisation
         if out.dtype != q_dtype:
             out = out.to(q_dtype)
-        if self.check_status and on_host:
+        nbytes = out.numel() * out.element_size()
+        if self._stage_out is None or self._stage_out.numel() < nbytes:
+            self._stage_out = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, pin_memory=True)
+        oh = self._stage_out[:nbytes].view(out.dtype).view(out.shape)
+        oh.copy_(out, non_blocking=True)
+        self._status_host.copy_(self.pool.status, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        if self.check_status and int(self._status_host[0]):
             self.pool.check_status()
-        for n in range(len(items)):
-            results[base + n] = out[n:n + 1]
+        res = oh.clone()
+        for n in range(B):
+            results[base + n] = res[n:n + 1]
 
     # ------------------------------------------------------------ tensor API
     def decode_batch(self, request_ids: Sequence[str], layer_idx: int, query: torch.Tensor,
@@ -245,14 +314,24 @@ class B200AttentionBackend:
         returns [T, Hq, D] on the GPU in the query dtype (all heads: sharded
         backends all-gather).  Enqueued on the current stream; no host sync.
         """
-        pool = self.pool
-        if pool is None:
-            raise KeyError("no request has been initialised")
         B = len(request_ids)
         n_new = [1] * B if n_new is None else [int(n) for n in n_new]
         T = sum(n_new)
         if query.shape[0] != T or key.shape[0] != T or value.shape[0] != T:
             raise ValueError(f"expected {T} new tokens, got q {tuple(query.shape)} k {tuple(key.shape)}")
+        reqs, rows, targets, offs, ctx_rows = self._plan(request_ids, layer_idx, n_new, query.shape[1:])
+        meta = to_device_i32(rows + offs + ctx_rows, self.device)
+        out = self._launch(reqs, layer_idx, n_new, targets, query, key, value, meta[0:B],
+                           meta[B:2 * B + 1], meta[2 * B + 1:], score_scale)
+        # the fused gather's buffer is rewritten by the next call
+        return out.clone() if self._peer is not None and out.data_ptr() == self._peer.out.data_ptr() else out
+
+    def _plan(self, request_ids, layer_idx: int, n_new, q_shape):
+        """Validate, reserve blocks for the new tokens and build the metadata
+        lists (rows, causal limits).  Raises before any state changes."""
+        pool = self.pool
+        if pool is None:
+            raise KeyError("no request has been initialised")
         reqs = []
         for r in request_ids:
             try:
@@ -261,23 +340,25 @@ class B200AttentionBackend:
                 raise KeyError(f"Unknown request {r}") from None
         if not 0 <= layer_idx < self.num_layers:
             raise IndexError(f"layer_idx {layer_idx} out of range [0, {self.num_layers})")
-        hq = query.shape[1]
-        if hq % self.num_kv_heads or query.shape[2] != self.head_dim:
-            raise ValueError(f"query {tuple(query.shape)} does not fit {self.num_kv_heads} KV heads x {self.head_dim}")
-        group = hq // self.num_kv_heads
+        hq, d = int(q_shape[0]), int(q_shape[1])
+        if hq % self.num_kv_heads or d != self.head_dim:
+            raise ValueError(f"query heads x dim {hq} x {d} do not fit {self.num_kv_heads} KV heads x {self.head_dim}")
         rows = [r.row for r in reqs]
         pos = [r.layer_len[layer_idx] for r in reqs]
         targets = [p + n for p, n in zip(pos, n_new)]
         pool.reserve(rows, targets, "OOM during append")
-
         offs = [0]
         ctx_rows: List[int] = []
         for p, n in zip(pos, n_new):
             offs.append(offs[-1] + n)
             ctx_rows.extend(range(p + 1, p + n + 1))
-        meta = to_device_i32(rows + offs + ctx_rows, self.device)
-        rows_d, offs_d, ctx_d = meta[0:B], meta[B:2 * B + 1], meta[2 * B + 1:]
+        return reqs, rows, targets, offs, ctx_rows
 
+    def _launch(self, reqs, layer_idx, n_new, targets, query, key, value, rows_d, offs_d, ctx_d,
+                score_scale):
+        pool = self.pool
+        hq = query.shape[1]
+        group = hq // self.num_kv_heads
         lo, hi = self.kv_range
         q = query.to(self.device, non_blocking=True)
         if q.dtype not in (torch.float32, self.kv_dtype):
@@ -286,23 +367,50 @@ class B200AttentionBackend:
             q = q[:, lo * group:hi * group]
         if q.stride(2) != 1 or q.stride(1) != self.head_dim:
             q = q.contiguous()
-        # one launch: append each row's token at ctx - 1, then attend (+ reduce)
-        out = pool.decode_step(layer_idx, q, self._local_kv(key), self._local_kv(value), offs_d,
-                               ctx_d, rows_d, max(n_new), max(targets), score_scale,
-                               partition_tokens=self.partition_tokens)
+        sharded = self.shard is not None and self.shard.world > 1
+        peer = self._peer_for(q) if sharded else None
+        if peer is not None:
+            # fused append + decode + reduce with the all-gather over NVLink
+            out = pool.decode_step_gather(layer_idx, q, self._local_kv(key), self._local_kv(value),
+                                          offs_d, ctx_d, rows_d, max(n_new), max(targets),
+                                          score_scale, peer, partition_tokens=self.partition_tokens)
+        else:
+            # one launch: append each row's token at ctx - 1, then attend (+ reduce)
+            out = pool.decode_step(layer_idx, q, self._local_kv(key), self._local_kv(value), offs_d,
+                                   ctx_d, rows_d, max(n_new), max(targets), score_scale,
+                                   partition_tokens=self.partition_tokens)
         for r, n in zip(reqs, n_new):
             r.layer_len[layer_idx] += n
             if layer_idx == self.num_layers - 1:
                 r.ctx += n
         st = self.stats
         st.batches += 1
-        st.items += B
-        st.tokens += T
-        esz = torch.empty((), dtype=self.kv_dtype).element_size()
-        st.kv_bytes_read += sum(targets) * (hi - lo) * self.head_dim * 2 * esz
-        if self.shard is not None and self.shard.world > 1:
+        st.items += len(reqs)
+        st.tokens += sum(n_new)
+        st.kv_bytes_read += sum(targets) * (hi - lo) * self.head_dim * 2 * self._kv_esz
+        if sharded and peer is None:
             out = self.shard.gather(out, self.num_kv_heads, group)
         return out
+
+    def _peer_for(self, q: torch.Tensor):
+        """The fused-gather buffers for this call's shape, or None (NCCL)."""
+        if self.gather_mode != "peer" or q.shape[0] > self.max_rows_per_call:
+            return None
+        if self.num_kv_heads % self.shard.world:
+            return None  # uneven shards: NCCL gather pads them
+        if self._peer is None:
+            from .sharded import PeerGather
+            self._peer = PeerGather(self.shard, self.max_rows_per_call,
+                                    q.shape[1] * self.shard.world, self.head_dim, q.dtype,
+                                    self.device)
+        return self._peer if self._peer.out.dtype == q.dtype else None
+
+    def close(self) -> None:
+        """Release the fused-gather peer buffers (collective under sharding:
+        every rank calls it)."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
 
     # ------------------------------------------------------------ debug
     def get_debug_info(self) -> dict:

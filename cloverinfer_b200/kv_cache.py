@@ -188,6 +188,24 @@ class PagedKVPool:
                          status=self.status)
         return out
 
+    def decode_step_gather(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                           query_start_loc: torch.Tensor, ctx_lens: torch.Tensor,
+                           seq_rows: Optional[torch.Tensor], max_q: int, max_ctx: int,
+                           score_scale: float, gather, partition_tokens: int = 0) -> torch.Tensor:
+        """decode_step for a head-sharded group: the all-gathered output of
+        every rank lands in ``gather.out`` (returned view, valid until the next call)."""
+        n_seqs = query_start_loc.numel() - 1
+        nbytes = _lib.decode_gather_workspace_bytes(n_seqs, q.shape[0], max_q, max_ctx, q.shape[1],
+                                                    self.num_kv_heads, self.head_dim,
+                                                    self.block_size, self.dtype, q.dtype,
+                                                    partition_tokens)
+        _lib.decode_step_gather(q, self.k[layer], self.v[layer], k_new, v_new, self.tables,
+                                query_start_loc, ctx_lens, gather, max_queries_per_seq=max_q,
+                                max_ctx_len=max_ctx, score_scale=score_scale, seq_rows=seq_rows,
+                                partition_tokens=partition_tokens, workspace=self.workspace(nbytes),
+                                status=self.status)
+        return gather.out[:q.shape[0]]
+
     # ------------------------------------------------------------ checks / views
     def check_status(self) -> None:
         """Raise if any kernel flagged a bad index since the last check (syncs)."""

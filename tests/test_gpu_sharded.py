@@ -100,6 +100,28 @@ def _worker(rank, world, port, q_out):
         nccl = sg.gather(outl, hkv, grp)
         torch.cuda.synchronize(dev)
         errs.append(float((nccl - ref).abs().max()))
+        # the drop-in backend, sharded, through decode_layer_batch with host items
+        from cloverinfer_b200 import B200AttentionBackend
+        gen = torch.Generator().manual_seed(9)
+        kv = {rid: [{"key": torch.randn(n, hkv, D, generator=gen).bfloat16(),
+                     "value": torch.randn(n, hkv, D, generator=gen).bfloat16()} for _ in range(2)]
+              for rid, n in [("a", 1200), ("b", 90)]}
+        bes = [B200AttentionBackend(device=dev, num_blocks=256, num_kv_heads=hkv, max_seqs=4),
+               B200AttentionBackend(device=dev, num_blocks=256, num_kv_heads=hkv, max_seqs=4,
+                                    shard=sg, gather="peer")]
+        for be in bes:
+            for rid, layers in kv.items():
+                be.init_request(rid, layers)
+        for layer in range(2):
+            items = [{"request_id": rid, "layer_idx": layer, "score_scale": 1 / math.sqrt(D),
+                      "query": torch.randn(hq, D, generator=gen),
+                      "key": torch.randn(hkv, D, generator=gen).bfloat16(),
+                      "value": torch.randn(hkv, D, generator=gen).bfloat16()} for rid in kv]
+            o0 = bes[0].decode_layer_batch(items)
+            o1 = bes[1].decode_layer_batch(items)
+            errs.append(max(float((x - y).abs().max()) for x, y in zip(o0, o1)))
+        assert bes[1]._peer is not None
+        bes[1].close()
         q_out.put((rank, int(st.item()), errs))
     except Exception as e:
         q_out.put((rank, -1, repr(e)))
