@@ -198,8 +198,10 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------ B200 arm
-def build_step(cfg, rank, world, lens, device, seed=0, gather=None):
-    """Pool + static buffers for one decode step at the configured contexts."""
+def build_step(cfg, rank, world, lens, device, seed=0, gather=None, n_new=None):
+    """Pool + static buffers for one decode step: sequence b holds lens[b]
+    tokens after the step, n_new[b] of them (default 1) appended by it and
+    attended causally."""
     from cloverinfer_b200 import _lib
     from cloverinfer_b200.head_groups import kv_head_shards
     from cloverinfer_b200.kv_cache import PagedKVPool
@@ -208,6 +210,8 @@ def build_step(cfg, rank, world, lens, device, seed=0, gather=None):
     hkv_l = hi - lo
     hq_l = hkv_l * cfg.group
     B, bs, D, dt = len(lens), cfg.block_size, cfg.head_dim, cfg.dtype
+    n_new = [1] * B if n_new is None else list(n_new)
+    T = sum(n_new)
     blocks = sum(-(-n // bs) for n in lens) + 64
     pool = PagedKVPool(blocks, bs, hkv_l, D, num_layers=1, dtype=dt, device=device,
                        max_seqs=B, max_blocks_per_seq=max(-(-n // bs) for n in lens) + 1)
@@ -217,75 +221,73 @@ def build_step(cfg, rank, world, lens, device, seed=0, gather=None):
     for t in (pool.k, pool.v):  # fill the whole pool: every block holds N(0,1)*scale data
         t.normal_(0.0, cfg.value_scale, generator=g) if dt == torch.float32 else \
             t.copy_(torch.randn(t.shape, generator=g, device=device).mul_(cfg.value_scale).to(dt))
-    q = (torch.randn((B, hq_l, D), generator=g, device=device) * cfg.value_scale).to(dt).float()
-    kn = (torch.randn((B, hkv_l, D), generator=g, device=device) * cfg.value_scale).to(dt)
-    vn = (torch.randn((B, hkv_l, D), generator=g, device=device) * cfg.value_scale).to(dt)
+    q = (torch.randn((T, hq_l, D), generator=g, device=device) * cfg.value_scale).to(dt).float()
+    kn = (torch.randn((T, hkv_l, D), generator=g, device=device) * cfg.value_scale).to(dt)
+    vn = (torch.randn((T, hkv_l, D), generator=g, device=device) * cfg.value_scale).to(dt)
+    max_q = max(n_new)
     # the configuration's split at N=1; with fewer KV heads per GPU the
-    # library's own choice keeps two waves of CTAs on the GPU
+    # library's own choice keeps the CTA waves full
     pt = cfg.partition_tokens if world == 1 else 0
-    pt = _lib.decode_partition_tokens(B, B, 1, max(lens), hq_l, hkv_l, D, bs, dt, torch.float32, pt)
-    meta = torch.tensor(list(range(B)) + [n - 1 for n in lens] + list(range(B + 1)) + list(lens),
-                        dtype=torch.int32, device=device)
-    rows, pos, offs, ctx = meta[:B], meta[B:2 * B], meta[2 * B:3 * B + 1], meta[3 * B + 1:]
-    slots = torch.empty(B, dtype=torch.int64, device=device)
+    pt = _lib.decode_partition_tokens(B, T, max_q, max(lens), hq_l, hkv_l, D, bs, dt, torch.float32, pt)
+    offs, ctx = [0], []
+    for n, k in zip(lens, n_new):
+        offs.append(offs[-1] + k)
+        ctx += list(range(n - k + 1, n + 1))
+    meta = torch.tensor(list(range(B)) + offs + ctx, dtype=torch.int32, device=device)
+    rows, offs_d, ctx_d = meta[:B], meta[B:2 * B + 1], meta[2 * B + 1:]
     out = torch.empty_like(q)
     if gather is not None:
-        nbytes = _lib.decode_gather_workspace_bytes(B, B, 1, max(lens), hq_l, hkv_l, D, bs, dt,
+        nbytes = _lib.decode_gather_workspace_bytes(B, T, max_q, max(lens), hq_l, hkv_l, D, bs, dt,
                                                     q.dtype, pt)
     else:
-        nbytes = _lib.decode_workspace_bytes(B, B, 1, max(lens), hq_l, hkv_l, D, bs, dt, q.dtype, pt)
+        nbytes = _lib.decode_workspace_bytes(B, T, max_q, max(lens), hq_l, hkv_l, D, bs, dt, q.dtype, pt)
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+    common = dict(max_queries_per_seq=max_q, max_ctx_len=max(lens), score_scale=cfg.score_scale,
+                  seq_rows=rows, partition_tokens=pt, workspace=ws, status=pool.status)
 
     def decode_only():
-        _lib.paged_decode(out, q, pool.k[0], pool.v[0], pool.tables, offs, ctx,
-                          max_queries_per_seq=1, max_ctx_len=max(lens), score_scale=cfg.score_scale,
-                          seq_rows=rows, partition_tokens=pt, workspace=ws,
-                          status=pool.status)
+        _lib.paged_decode(out, q, pool.k[0], pool.v[0], pool.tables, offs_d, ctx_d, **common)
 
     def step():
         if gather is not None:
             # fused append + decode, then reduce with the all-gather fused in
-            _lib.decode_step_gather(q, pool.k[0], pool.v[0], kn, vn, pool.tables, offs, ctx, gather,
-                                    max_queries_per_seq=1, max_ctx_len=max(lens),
-                                    score_scale=cfg.score_scale, seq_rows=rows, partition_tokens=pt,
-                                    workspace=ws, status=pool.status)
+            _lib.decode_step_gather(q, pool.k[0], pool.v[0], kn, vn, pool.tables, offs_d, ctx_d,
+                                    gather, **common)
             return
-        # append each sequence's new token at position ctx-1 and attend (fused)
-        _lib.decode_step(out, q, pool.k[0], pool.v[0], kn, vn, pool.tables, offs, ctx,
-                         max_queries_per_seq=1, max_ctx_len=max(lens), score_scale=cfg.score_scale,
-                         seq_rows=rows, partition_tokens=pt, workspace=ws,
-                         status=pool.status)
+        # append each row's new token at position ctx-1 and attend (fused)
+        _lib.decode_step(out, q, pool.k[0], pool.v[0], kn, vn, pool.tables, offs_d, ctx_d, **common)
 
     return dict(pool=pool, q=q, out=out, step=step, decode_only=decode_only, hkv_local=hkv_l,
-                hq_local=hq_l, kv_range=(lo, hi), partition_tokens=pt, workspace_bytes=nbytes)
+                hq_local=hq_l, kv_range=(lo, hi), partition_tokens=pt, workspace_bytes=nbytes,
+                rows=T, max_q=max_q)
 
 
 def run_b200(args):
     from cloverinfer_b200 import _lib
-    from cloverinfer_b200.workloads import CONFIGS, context_lengths, kv_bytes
+    from cloverinfer_b200.workloads import CONFIGS, context_lengths, kv_bytes, new_tokens
 
     rank, world, local = _dist_setup()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     _lib.lib()
     cfg = CONFIGS[args.config]
-    lens = context_lengths(cfg, 0)
-    if args.batch:
-        lens = (lens * (args.batch // len(lens) + 1))[:args.batch]
+    lens = context_lengths(cfg, 0, args.batch)
+    n_new = new_tokens(cfg, 0, args.batch)
     B = len(lens)
+    T = sum(n_new)
     total_kv = kv_bytes(lens, cfg.num_kv_heads, cfg.head_dim, cfg.dtype)
     peer = None
     if world > 1 and args.gather == "peer":
         from cloverinfer_b200.head_groups import kv_head_shards
         from cloverinfer_b200.sharded import HeadShardGroup, PeerGather
         lo, hi = kv_head_shards(cfg.num_kv_heads, world)[rank]
-        peer = PeerGather(HeadShardGroup(), B, cfg.num_q_heads, cfg.head_dim, torch.float32, device)
-    st = build_step(cfg, rank, world, lens, device, gather=peer)
+        peer = PeerGather(HeadShardGroup(), T, cfg.num_q_heads, cfg.head_dim, torch.float32, device)
+    st = build_step(cfg, rank, world, lens, device, gather=peer, n_new=n_new)
     local_kv = kv_bytes(lens, st["hkv_local"], cfg.head_dim, cfg.dtype)
     gather = None
     if world > 1 and peer is None:
         import torch.distributed as dist
-        recv = torch.empty((world, B, st["hq_local"], cfg.head_dim), dtype=st["out"].dtype, device=device)
+        recv = torch.empty((world * T, st["hq_local"], cfg.head_dim), dtype=st["out"].dtype, device=device)
 
         def gather():
             dist.all_gather_into_tensor(recv, st["out"])
@@ -363,7 +365,7 @@ def run_b200(args):
     torch.cuda.synchronize(device)
 
     # ---------------- e2e through the public API (host buffers in, host out)
-    e2e = run_e2e(cfg, lens, rank, world, device, args)
+    e2e = run_e2e(cfg, lens, n_new, rank, world, device, args)
 
     hbm_peak, peak_kind = _peaks()
     achieved = local_kv / (dec_ms * 1e-3) / 1e9
@@ -374,7 +376,7 @@ def run_b200(args):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16" if cfg.dtype == torch.bfloat16 else str(cfg.dtype).replace("torch.", ""),
         "data": "synthetic",
-        "config": {"workload": cfg.name, "batch": B, "ctx": f"{cfg.ctx_lo}-{cfg.ctx_hi}",
+        "config": {"workload": cfg.name, "batch": B, "new_tokens": T, "ctx": f"{cfg.ctx_lo}-{cfg.ctx_hi}",
                    "num_q_heads": cfg.num_q_heads, "num_kv_heads": cfg.num_kv_heads,
                    "head_dim": cfg.head_dim, "block_size": cfg.block_size,
                    "partition_tokens": st["partition_tokens"],
@@ -382,7 +384,7 @@ def run_b200(args):
                    "cuda_graph": used_graph,
                    "l2": "inputs > L2 (KV %.0f MB per GPU)" % (local_kv / 1e6)},
         "steps_per_s": round(1e3 / ms, 2),
-        "tokens_per_s": round(B * 1e3 / ms, 2),
+        "tokens_per_s": round(T * 1e3 / ms, 2),
         "pct_hbm_peak_per_gpu": round(100.0 * value / world / hbm_peak, 2),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "traffic": None,
@@ -409,64 +411,77 @@ def run_b200(args):
         dist.destroy_process_group()
 
 
-def run_e2e(cfg, lens, rank, world, device, args):
-    """decode_layer_batch with per-item host tensors (pinned), as AttentionNode calls it."""
+def run_e2e(cfg, lens, n_new, rank, world, device, args):
+    """The public API with host tensors: decode_layer_batch (per-item tensors, as
+    AttentionNode calls it) for one new token per sequence, decode_batch (host
+    [T, H, D] tensors) for multi-token steps."""
     from cloverinfer_b200 import B200AttentionBackend, HeadShardGroup
     from cloverinfer_b200.workloads import kv_bytes
     shard = HeadShardGroup() if world > 1 else None
     B, D, dt = len(lens), cfg.head_dim, cfg.dtype
-    be = B200AttentionBackend(num_blocks=sum(-(-(n + args.steps + args.warmup + 16) // cfg.block_size)
+    T = sum(n_new)
+    steps_total = args.steps + args.warmup
+    be = B200AttentionBackend(num_blocks=sum(-(-(n + 4 * steps_total + 16) // cfg.block_size)
                                              for n in lens) + 64,
                               block_size=cfg.block_size, num_kv_heads=cfg.num_kv_heads, kv_dtype=dt,
                               device=device, max_seqs=B, shard=shard, shuffle_seed=77,
                               partition_tokens=cfg.partition_tokens if world == 1 else 0,
-                              max_seq_len=max(lens) + 4096, gather=args.gather,
-                              max_rows_per_call=B)
+                              max_seq_len=max(lens) + 4 * steps_total + 4096, gather=args.gather,
+                              max_rows_per_call=T)
     g = torch.Generator(device=device).manual_seed(99)
     lo, hi = (0, cfg.num_kv_heads) if shard is None else shard.kv_range(cfg.num_kv_heads)
-    for i, n in enumerate(lens):
+    for i, (n, k) in enumerate(zip(lens, n_new)):
         # prefill KV built on the device for speed; heads outside this rank's
         # shard are never read, so they are left as zeros
-        k = torch.zeros((n - 1, cfg.num_kv_heads, D), dtype=dt, device=device)
-        v = torch.zeros_like(k)
-        k[:, lo:hi] = (torch.randn((n - 1, hi - lo, D), generator=g, device=device) * cfg.value_scale).to(dt)
-        v[:, lo:hi] = (torch.randn((n - 1, hi - lo, D), generator=g, device=device) * cfg.value_scale).to(dt)
-        be.init_request(f"r{i}", [{"key": k, "value": v}])
-        del k, v
+        kk = torch.zeros((n - k, cfg.num_kv_heads, D), dtype=dt, device=device)
+        vv = torch.zeros_like(kk)
+        kk[:, lo:hi] = (torch.randn((n - k, hi - lo, D), generator=g, device=device) * cfg.value_scale).to(dt)
+        vv[:, lo:hi] = (torch.randn((n - k, hi - lo, D), generator=g, device=device) * cfg.value_scale).to(dt)
+        be.init_request(f"r{i}", [{"key": kk, "value": vv}])  # one layer: a step is one layer
+        del kk, vv
     hg = torch.Generator().manual_seed(5)
-    items = []
-    for i in range(B):
-        items.append({"request_id": f"r{i}", "layer_idx": 0,
-                      "query": torch.randn((cfg.num_q_heads, D), generator=hg).pin_memory(),
-                      "key": torch.randn((cfg.num_kv_heads, D), generator=hg).to(dt).pin_memory(),
-                      "value": torch.randn((cfg.num_kv_heads, D), generator=hg).to(dt).pin_memory(),
-                      "score_scale": cfg.score_scale})
-    h2d = sum(it["query"].numel() * 4 + 2 * it["key"].numel() * it["key"].element_size() for it in items)
-    d2h = B * cfg.num_q_heads * D * 4
+    ids = [f"r{i}" for i in range(B)]
+    single = all(k == 1 for k in n_new)
+    if single:
+        items = [{"request_id": rid, "layer_idx": 0,
+                  "query": torch.randn((cfg.num_q_heads, D), generator=hg).pin_memory(),
+                  "key": torch.randn((cfg.num_kv_heads, D), generator=hg).to(dt).pin_memory(),
+                  "value": torch.randn((cfg.num_kv_heads, D), generator=hg).to(dt).pin_memory(),
+                  "score_scale": cfg.score_scale} for rid in ids]
+        call = lambda: be.decode_layer_batch(items)  # noqa: E731
+    else:
+        qh = torch.randn((T, cfg.num_q_heads, D), generator=hg).pin_memory()
+        kh = torch.randn((T, cfg.num_kv_heads, D), generator=hg).to(dt).pin_memory()
+        vh = torch.randn((T, cfg.num_kv_heads, D), generator=hg).to(dt).pin_memory()
+        call = lambda: be.decode_batch(ids, 0, qh, kh, vh, cfg.score_scale, n_new=n_new).cpu()  # noqa: E731
+    esz = torch.empty((), dtype=dt).element_size()
+    h2d = T * cfg.num_q_heads * D * 4 + 2 * T * cfg.num_kv_heads * D * esz
+    d2h = T * cfg.num_q_heads * D * 4
     for _ in range(args.warmup):
-        be.decode_layer_batch(items)
+        call()
     torch.cuda.synchronize(device)
     _barrier(world)
-    lens_before = [be.get_context_len(f"r{i}") for i in range(B)]
+    lens_before = [be.get_context_len(rid) for rid in ids]
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        be.decode_layer_batch(items)
+        call()
     e1.record()
     torch.cuda.synchronize(device)
     ms = _max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
-    # bytes actually attended over (contexts grow by one token per step)
-    attended = sum(kv_bytes([n + 1 + s for n in lens_before], cfg.num_kv_heads, D, dt)
-                   for s in range(args.steps)) / args.steps
-    for i in range(B):
-        be.free_request(f"r{i}")
+    # bytes actually attended over (contexts grow by n_new tokens per step)
+    attended = sum(kv_bytes([n + (s + 1) * k for n, k in zip(lens_before, n_new)],
+                            cfg.num_kv_heads, D, dt) for s in range(args.steps)) / args.steps
+    for rid in ids:
+        be.free_request(rid)
     be.close()
     del be
     torch.cuda.empty_cache()
     return {"value": round(attended / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 5),
-            "api": "B200AttentionBackend.decode_layer_batch (per-item host tensors)",
+            "api": ("B200AttentionBackend.decode_layer_batch (per-item host tensors)" if single
+                    else "B200AttentionBackend.decode_batch (host tensors, multi-token)"),
             "gather": "none" if world == 1 else args.gather}
 
 

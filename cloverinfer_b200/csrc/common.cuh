@@ -35,6 +35,15 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// --- programmatic dependent launch (kernels launched with the PDL attribute) ---
+// Wait until the preceding kernel in the stream has completed and its memory
+// is visible (a no-op when launched without the attribute).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Let the next kernel in the stream start launching its CTAs.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // --- mbarrier (CTA scope) ---
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");

@@ -32,6 +32,8 @@
 #include <math.h>
 #include <cmath>
 #include <mutex>
+#include <stdlib.h>
+#include <utility>
 
 #include <cudaTypedefs.h>
 
@@ -346,8 +348,12 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   __shared__ __align__(8) uint64_t bars[NW * STAGES];
   __shared__ int s_abort;
 
+  pdl_wait();  // inputs, tables and workspace are final before anything is read
   CtaWork w;
-  if (!cta_work(a, w, D)) return;
+  if (!cta_work(a, w, D)) {
+    pdl_trigger();
+    return;
+  }
   if (a.k_new != nullptr && append_new_tokens(a, w, D)) fence_proxy_async_global();
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -587,7 +593,10 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
     l_b += __shfl_xor_sync(0xffffffffu, l_b, off);
   }
   __syncthreads();  // every warp is done with its ring: reuse it for the merge
-  if (s_abort) return;
+  if (s_abort) {
+    pdl_trigger();
+    return;
+  }
 
   float* red_acc = reinterpret_cast<float*>(smem);
   float* red_m = red_acc + NW * kMmaCols * (D + 4);
@@ -611,6 +620,7 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   }
   __syncthreads();
   merge_store_rt(a, w, red_acc, red_m, red_l, kMmaCols, D, NW);
+  pdl_trigger();  // the split-K reduce may launch once every CTA got here
 }
 
 // ------------------------------------------------------------------ SIMT path
@@ -621,8 +631,12 @@ paged_decode_simt_kernel(const DecodeArgs a, int D) {
   constexpr int DMAX = 32 * EPL;
   __shared__ float red_acc[kNumWarps * NC * (DMAX + 4)];
   __shared__ float red_m[kNumWarps * NC], red_l[kNumWarps * NC];
+  pdl_wait();
   CtaWork w;
-  if (!cta_work(a, w, D)) return;
+  if (!cta_work(a, w, D)) {
+    pdl_trigger();
+    return;
+  }
   if (a.k_new != nullptr && append_new_tokens(a, w, D)) __syncthreads();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -695,6 +709,7 @@ paged_decode_simt_kernel(const DecodeArgs a, int D) {
   }
   __syncthreads();
   merge_store_rt(a, w, red_acc, red_m, red_l, NC, D, kNumWarps);
+  pdl_trigger();
 }
 
 // ------------------------------------------------------------------ split-K reduce
@@ -707,51 +722,87 @@ constexpr int kReduceWarps = 4;
 constexpr int kReduceMaxParts = 1024;
 constexpr int kReduceDims = 32;
 
-__global__ void __launch_bounds__(kReduceWarps * 32)
+// Combine the partitions of one (query row, head) for one dim per lane.
+// Warp w takes partitions w, w+4, ..., all of whose log-sum-exp values and
+// partial outputs it loads at once (one memory round trip per 64
+// partitions), folding them into a running (max, sum, value); the four warps
+// are merged in shared memory.  Every thread of the CTA must call it; the
+// result is valid in warp 0.
+constexpr int kPartsPerWarp = 16;
+
+__device__ __forceinline__ float reduce_unit(const DecodeArgs& a, int r, int h, int dim, int D,
+                                             float* s_m, float* s_l,
+                                             float (*s_o)[kReduceDims]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lim = __ldg(a.ctx + r);
+  const int np = lim > 0 ? (lim + a.part_tokens - 1) / a.part_tokens : 0;
+  const int npp = np < a.max_parts ? np : a.max_parts;
+  const int64_t base = ((int64_t)r * a.num_q_heads + h) * a.max_parts;
+  float m = -INFINITY, l = 0.f, o = 0.f;
+  for (int p0 = 0; p0 < npp; p0 += kReduceWarps * kPartsPerWarp) {
+    float lv[kPartsPerWarp], ov[kPartsPerWarp];
+#pragma unroll
+    for (int i = 0; i < kPartsPerWarp; ++i) {
+      const int p = p0 + warp + i * kReduceWarps;
+      const bool ok = p < npp;
+      lv[i] = ok ? __ldcg(a.part_lse + base + p) : -INFINITY;
+      ov[i] = (ok && dim < D) ? __ldcg(a.part_out + (base + p) * D + dim) : 0.f;
+    }
+    float mm = m;
+#pragma unroll
+    for (int i = 0; i < kPartsPerWarp; ++i) mm = fmaxf(mm, lv[i]);
+    const float u = mm == -INFINITY ? 0.f : mm;
+    const float sc = fast_exp2(m - u);
+    l *= sc;
+    o *= sc;
+#pragma unroll
+    for (int i = 0; i < kPartsPerWarp; ++i) {
+      const float e = fast_exp2(lv[i] - u);
+      l += e;
+      o = fmaf(e, ov[i], o);
+    }
+    m = mm;
+  }
+  if (lane == 0) {
+    s_m[warp] = m;
+    s_l[warp] = l;
+  }
+  s_o[warp][lane] = o;
+  __syncthreads();
+  float v = 0.f;
+  if (warp == 0) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < kReduceWarps; ++k) M = fmaxf(M, s_m[k]);
+    if (M != -INFINITY) {
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int k = 0; k < kReduceWarps; ++k) {
+        const float e = fast_exp2(s_m[k] - M);
+        L += s_l[k] * e;
+        O = fmaf(s_o[k][lane], e, O);
+      }
+      v = L > 0.f ? O / L : 0.f;
+    }
+  }
+  __syncthreads();  // shared scratch is reused by the caller's next unit
+  return v;
+}
+
+__global__ void __launch_bounds__(kReduceWarps * 32, 6)
 splitk_reduce_kernel(const DecodeArgs a, int D) {
-  __shared__ float s_w[kReduceMaxParts];
-  __shared__ float s_red[kReduceWarps][kReduceDims];
-  __shared__ float s_wmax[kReduceWarps], s_wsum[kReduceWarps];
+  __shared__ float s_m[kReduceWarps], s_l[kReduceWarps];
+  __shared__ float s_o[kReduceWarps][kReduceDims];
+  pdl_wait();     // every partial of the decode kernel is written
+  pdl_trigger();  // the next step's kernel may start launching (it waits too)
   const int r = blockIdx.x;
   const int h = blockIdx.y;
   const int lim = __ldg(a.ctx + r);
-  const int np = (lim + a.part_tokens - 1) / a.part_tokens;
-  if (np <= 1) return;  // written (or zero-filled) by the decode kernel
-  const int npp = min(min(np, a.max_parts), kReduceMaxParts);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t base = ((int64_t)r * a.num_q_heads + h) * a.max_parts;
-  const float* lse = a.part_lse + base;
-  float M = -INFINITY;
-  for (int p = threadIdx.x; p < npp; p += blockDim.x) M = fmaxf(M, __ldcg(lse + p));
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  if (lane == 0) s_wmax[warp] = M;
-  __syncthreads();
-  M = fmaxf(fmaxf(s_wmax[0], s_wmax[1]), fmaxf(s_wmax[2], s_wmax[3]));
-  float L = 0.f;
-  for (int p = threadIdx.x; p < npp; p += blockDim.x) {
-    const float wt = M == -INFINITY ? 0.f : fast_exp2(__ldcg(lse + p) - M);
-    s_w[p] = wt;
-    L += wt;
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-  if (lane == 0) s_wsum[warp] = L;
-  __syncthreads();
-  L = (s_wsum[0] + s_wsum[1]) + (s_wsum[2] + s_wsum[3]);
+  if ((lim + a.part_tokens - 1) / a.part_tokens <= 1) return;  // written by the decode kernel
+  const int lane = threadIdx.x & 31;
   const int dim = blockIdx.z * kReduceDims + lane;
-  float o = 0.f;
-  if (dim < D) {
-    const float* po = a.part_out + base * D + dim;
-#pragma unroll 8
-    for (int p = warp; p < npp; p += kReduceWarps) o = fmaf(s_w[p], __ldcg(po + (int64_t)p * D), o);
-  }
-  s_red[warp][lane] = o;
-  __syncthreads();
-  if (warp == 0 && dim < D) {
-    const float v = (s_red[0][lane] + s_red[1][lane]) + (s_red[2][lane] + s_red[3][lane]);
-    store_out(a, (int64_t)r * a.out_stride + (int64_t)h * D + dim, L > 0.f ? v / L : 0.f);
-  }
+  const float v = reduce_unit(a, r, h, dim, D, s_m, s_l, s_o);
+  if (threadIdx.x < 32 && dim < D) store_out(a, (int64_t)r * a.out_stride + (int64_t)h * D + dim, v);
 }
 
 // Split-K reduce with the output all-gather fused in.  A unit is (query row,
@@ -775,10 +826,11 @@ __device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
 
 __global__ void __launch_bounds__(kReduceWarps * 32)
 reduce_gather_kernel(const DecodeArgs a, const GatherArgs g, int D) {
-  __shared__ float s_w[kReduceMaxParts];
-  __shared__ float s_red[kReduceWarps][kReduceDims];
-  __shared__ float s_wmax[kReduceWarps], s_wsum[kReduceWarps];
+  __shared__ float s_m[kReduceWarps], s_l[kReduceWarps];
+  __shared__ float s_o[kReduceWarps][kReduceDims];
   __shared__ int s_last;
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int epoch = *(volatile int32_t*)(g.sync + kSyncEpoch) + 1;
   const int64_t half = (int64_t)(epoch & 1) * g.ll_half_words;
@@ -790,46 +842,13 @@ reduce_gather_kernel(const DecodeArgs a, const GatherArgs g, int D) {
     const int dc = u % dchunks;
     const int h = (u / dchunks) % heads;
     const int r = u / (dchunks * heads);
-    const int lim = __ldg(a.ctx + r);
-    const int np = lim > 0 ? (lim + a.part_tokens - 1) / a.part_tokens : 0;
-    const int npp = min(min(np, a.max_parts), kReduceMaxParts);
-    const int64_t base = ((int64_t)r * heads + h) * a.max_parts;
-    const float* lse = a.part_lse + base;
-    float M = -INFINITY;
-    for (int p = threadIdx.x; p < npp; p += blockDim.x) M = fmaxf(M, __ldcg(lse + p));
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    if (lane == 0) s_wmax[warp] = M;
-    __syncthreads();
-    M = fmaxf(fmaxf(s_wmax[0], s_wmax[1]), fmaxf(s_wmax[2], s_wmax[3]));
-    float L = 0.f;
-    for (int p = threadIdx.x; p < npp; p += blockDim.x) {
-      const float wt = M == -INFINITY ? 0.f : fast_exp2(__ldcg(lse + p) - M);
-      s_w[p] = wt;
-      L += wt;
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-    if (lane == 0) s_wsum[warp] = L;
-    __syncthreads();
-    L = (s_wsum[0] + s_wsum[1]) + (s_wsum[2] + s_wsum[3]);
     const int dim = dc * kReduceDims + lane;
-    float o = 0.f;
-    if (dim < D) {
-      const float* po = a.part_out + base * D + dim;
-#pragma unroll 8
-      for (int p = warp; p < npp; p += kReduceWarps) o = fmaf(s_w[p], __ldcg(po + (int64_t)p * D), o);
-    }
-    s_red[warp][lane] = o;
-    __syncthreads();
+    const float v = reduce_unit(a, r, h, dim, D, s_m, s_l, s_o);
     if (warp == 0 && dim < D) {
-      const float v =
-          L > 0.f ? ((s_red[0][lane] + s_red[1][lane]) + (s_red[2][lane] + s_red[3][lane])) / L : 0.f;
       const uint64_t word = ((uint64_t)(uint32_t)epoch << 32) | (uint64_t)__float_as_uint(v);
       const int64_t idx = half + ((int64_t)r * g.total_q_heads + g.q_head_offset + h) * D + dim;
       for (int rr = 0; rr < g.n_ranks; ++rr) st_relaxed_sys_u64(g.peer_ll[rr] + idx, word);
     }
-    __syncthreads();  // shared buffers are reused by the next unit
   }
 
   // ---- phase 2: receive every rank's words for this CTA's units
@@ -970,6 +989,31 @@ static int choose_partition(int max_ctx, int BS, int rows_x_kvh, bool mma) {
   return pt;
 }
 
+// Programmatic dependent launch: on by default; CLOVER_B200_PDL=0 turns it off.
+static bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("CLOVER_B200_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 template <typename Kern>
 static int set_smem(Kern k, int bytes) {
   static std::mutex mu;
@@ -992,8 +1036,8 @@ static int launch_mma(const DecodeArgs& a, const CUtensorMap& tk, const CUtensor
     if (rc) return rc;
     if (dev < 64) configured |= 1ull << dev;
   }
-  kern<<<grid, kMmaThreads, G::kSmem, s>>>(tk, tv, a);
-  return check_cuda(cudaGetLastError(), "paged_decode_mma launch");
+  return check_cuda(launch_pdl(kern, grid, dim3(kMmaThreads), G::kSmem, s, tk, tv, a),
+                    "paged_decode_mma launch");
 }
 
 template <typename T, bool QF32, int D>
@@ -1015,13 +1059,14 @@ static int dispatch_d(int D, int BS, const DecodeArgs& a, const CUtensorMap& tk,
 
 template <typename KT, int EPL>
 static int launch_simt_nc(int nc, int D, const DecodeArgs& a, dim3 grid, cudaStream_t s) {
+  cudaError_t e;
   switch (nc) {
-    case 1: paged_decode_simt_kernel<KT, EPL, 1><<<grid, kThreads, 0, s>>>(a, D); break;
-    case 2: paged_decode_simt_kernel<KT, EPL, 2><<<grid, kThreads, 0, s>>>(a, D); break;
-    case 4: paged_decode_simt_kernel<KT, EPL, 4><<<grid, kThreads, 0, s>>>(a, D); break;
-    default: paged_decode_simt_kernel<KT, EPL, 8><<<grid, kThreads, 0, s>>>(a, D); break;
+    case 1: e = launch_pdl(paged_decode_simt_kernel<KT, EPL, 1>, grid, dim3(kThreads), 0, s, a, D); break;
+    case 2: e = launch_pdl(paged_decode_simt_kernel<KT, EPL, 2>, grid, dim3(kThreads), 0, s, a, D); break;
+    case 4: e = launch_pdl(paged_decode_simt_kernel<KT, EPL, 4>, grid, dim3(kThreads), 0, s, a, D); break;
+    default: e = launch_pdl(paged_decode_simt_kernel<KT, EPL, 8>, grid, dim3(kThreads), 0, s, a, D); break;
   }
-  return check_cuda(cudaGetLastError(), "paged_decode_simt launch");
+  return check_cuda(e, "paged_decode_simt launch");
 }
 
 template <typename KT>
@@ -1254,15 +1299,17 @@ static int decode_impl(
     if (cudaGetDevice(&dev) == cudaSuccess)
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int grid = g.units < sms * kGatherCtasPerSm ? g.units : sms * kGatherCtasPerSm;
-    reduce_gather_kernel<<<grid, kReduceWarps * 32, 0, s>>>(a, g, head_dim);
-    return check_cuda(cudaGetLastError(), "reduce_gather launch");
+    return check_cuda(launch_pdl(reduce_gather_kernel, dim3(grid), dim3(kReduceWarps * 32), 0, s,
+                                 a, g, head_dim),
+                      "reduce_gather launch");
   }
   if (max_parts > 1) {
     // Rows with several partitions are combined here; single-partition rows
     // were written by the decode kernel and return at once.
     const dim3 rgrid(n_query_rows, num_q_heads, (head_dim + kReduceDims - 1) / kReduceDims);
-    splitk_reduce_kernel<<<rgrid, kReduceWarps * 32, 0, s>>>(a, head_dim);
-    rc = check_cuda(cudaGetLastError(), "splitk_reduce launch");
+    rc = check_cuda(launch_pdl(splitk_reduce_kernel, rgrid, dim3(kReduceWarps * 32), 0, s, a,
+                               head_dim),
+                    "splitk_reduce launch");
   }
   return rc;
 }
