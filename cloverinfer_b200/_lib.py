@@ -41,6 +41,7 @@ _F = ctypes.c_float
 SIGNATURES = {
     "clover_b200_version": (ctypes.c_int, []),
     "clover_b200_last_error": (ctypes.c_char_p, []),
+    "clover_b200_host_gather": (ctypes.c_int, [_P, _P, _I32, _P]),
     "clover_b200_block_reserve": (ctypes.c_int, [_P, _P, _I32, _P, _I32, _P, _P, _P, _I32, _I32, _P, _P]),
     "clover_b200_block_free": (ctypes.c_int, [_P, _P, _I32, _P, _I32, _P, _P, _I32, _P, _P]),
     "clover_b200_compute_slots": (ctypes.c_int, [_P, _I32, _P, _P, _P, _I32, _I32, _I64, _P, _P, _P]),
@@ -236,13 +237,28 @@ def paged_decode(out, q, k_cache, v_cache, block_tables, query_start_loc, ctx_le
 
 def decode_step(out, q, k_cache, v_cache, k_new, v_new, block_tables, query_start_loc, ctx_lens, *,
                 max_queries_per_seq, max_ctx_len, score_scale, seq_rows=None,
-                partition_tokens=0, workspace=None, status=None):
+                partition_tokens=0, workspace=None, status=None, check=True):
     """Append row r's new token (k_new/v_new[r], [n_rows, Hkv, D]) at ctx_lens[r]-1, then
-    paged decode as :func:`paged_decode` — one launch when the append can be fused."""
-    _require_cuda(out, q, k_cache, v_cache, k_new, v_new, block_tables, query_start_loc,
-                  ctx_lens, seq_rows, workspace, status)
+    paged decode as :func:`paged_decode` — one launch when the append can be fused.
+    ``check=False`` skips the Python-side shape checks (callers that built the
+    tensors themselves); the library still validates sizes and pointers."""
     nb, bs, hkv, d = k_cache.shape
     rows, hq, dq = q.shape
+    if not check:
+        ws_bytes = 0 if workspace is None else workspace.numel()
+        rc = lib().clover_b200_decode_step(
+            out.data_ptr(), out.stride(0), q.data_ptr(), q.stride(0), _DTYPE[q.dtype],
+            k_cache.data_ptr(), v_cache.data_ptr(), _DTYPE[k_cache.dtype], nb, bs,
+            k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0), block_tables.data_ptr(),
+            block_tables.stride(0), _ptr(seq_rows), query_start_loc.data_ptr(), ctx_lens.data_ptr(),
+            query_start_loc.numel() - 1, rows, max_queries_per_seq, max_ctx_len, hq, hkv, d,
+            float(score_scale), partition_tokens, _ptr(workspace), ws_bytes, _ptr(status),
+            torch.cuda.current_stream(q.device).cuda_stream)
+        if rc != OK:
+            _check(rc, "clover_b200_decode_step")
+        return
+    _require_cuda(out, q, k_cache, v_cache, k_new, v_new, block_tables, query_start_loc,
+                  ctx_lens, seq_rows, workspace, status)
     if dq != d or out.shape != q.shape or out.dtype != q.dtype:
         raise ValueError("decode_step: q/out mismatch")
     if k_new.shape != (rows, hkv, d) or v_new.shape != k_new.shape:
@@ -336,3 +352,11 @@ def decode_step_gather(q, k_cache, v_cache, k_new, v_new, block_tables, query_st
         gather.peer_recv_d.data_ptr(), gather.sync.data_ptr(), gather.world, gather.rank,
         gather.half_words, _ptr(workspace), ws_bytes, _ptr(status), _stream(q.device))
     _check(rc, "clover_b200_decode_step_gather")
+
+
+def host_gather(srcs, sizes, n: int, dst_ptr: int) -> None:
+    """Copy n host buffers (ctypes arrays of pointers / byte counts) back to back into dst."""
+    rc = lib().clover_b200_host_gather(srcs, sizes, n, dst_ptr)
+    if rc != OK:
+        _check(rc, "clover_b200_host_gather")
+

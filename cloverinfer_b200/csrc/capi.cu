@@ -1,6 +1,7 @@
 // Library-wide C ABI pieces: version, last-error string, CUDA error mapping.
 #include <stdarg.h>
 #include <stdio.h>
+#include <string.h>
 
 #include "common.cuh"
 
@@ -24,5 +25,21 @@ int check_cuda(cudaError_t e, const char* what) {
 }  // namespace clover
 
 extern "C" int clover_b200_version(void) { return 100; }  // 0.1.0
+
+// Host-side gather of n source buffers into one destination (a pinned
+// staging buffer): one native call instead of one framework op per item.
+extern "C" int clover_b200_host_gather(const void* const* srcs, const int64_t* nbytes, int32_t n,
+                                       void* dst) {
+  if (n < 0 || (n > 0 && (!srcs || !nbytes || !dst)))
+    return clover::set_error(CLOVER_B200_ERR_INVALID_ARG, "host_gather: bad arguments");
+  char* d = static_cast<char*>(dst);
+  for (int32_t i = 0; i < n; ++i) {
+    if (nbytes[i] < 0 || (nbytes[i] > 0 && !srcs[i]))
+      return clover::set_error(CLOVER_B200_ERR_INVALID_ARG, "host_gather: bad source %d", i);
+    memcpy(d, srcs[i], (size_t)nbytes[i]);
+    d += nbytes[i];
+  }
+  return CLOVER_B200_OK;
+}
 
 extern "C" const char* clover_b200_last_error(void) { return clover::g_last_error; }

@@ -172,7 +172,8 @@ class PagedKVPool:
     def decode_step(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
                     query_start_loc: torch.Tensor, ctx_lens: torch.Tensor,
                     seq_rows: Optional[torch.Tensor], max_q: int, max_ctx: int, score_scale: float,
-                    out: Optional[torch.Tensor] = None, partition_tokens: int = 0) -> torch.Tensor:
+                    out: Optional[torch.Tensor] = None, partition_tokens: int = 0,
+                    check: bool = True) -> torch.Tensor:
         """Append every query row's new token at ctx - 1 and attend (one fused
         launch for a plain decode step).  Capacity must be reserved first."""
         if out is None:
@@ -185,7 +186,7 @@ class PagedKVPool:
                          query_start_loc, ctx_lens, max_queries_per_seq=max_q, max_ctx_len=max_ctx,
                          score_scale=score_scale, seq_rows=seq_rows,
                          partition_tokens=partition_tokens, workspace=self.workspace(nbytes),
-                         status=self.status)
+                         status=self.status, check=check)
         return out
 
     def decode_step_gather(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,

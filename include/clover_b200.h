@@ -69,6 +69,15 @@ CLOVER_B200_API int clover_b200_version(void);
 CLOVER_B200_API const char* clover_b200_last_error(void);
 
 /*
+ * Host helper: copy n host buffers back to back into dst (a pinned staging
+ * buffer), so a batch of per-request tensors becomes one H2D copy.
+ * Replaces: the per-item tensor hand-off of AttentionNode.decode_layer_batch
+ * (src/core/nodes.py:154) into the batched call; no device work.
+ */
+CLOVER_B200_API int clover_b200_host_gather(const void* const* srcs, const int64_t* nbytes,
+                                            int32_t n, void* dst);
+
+/*
  * Block allocator — the free-block stack and block tables of
  * KVCacheManager, resident in device memory.
  *
