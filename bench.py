@@ -199,67 +199,8 @@ def run_reference(args):
 
 # ------------------------------------------------------------------ B200 arm
 def build_step(cfg, rank, world, lens, device, seed=0, gather=None, n_new=None):
-    """Pool + static buffers for one decode step: sequence b holds lens[b]
-    tokens after the step, n_new[b] of them (default 1) appended by it and
-    attended causally."""
-    from cloverinfer_b200 import _lib
-    from cloverinfer_b200.head_groups import kv_head_shards
-    from cloverinfer_b200.kv_cache import PagedKVPool
-
-    lo, hi = kv_head_shards(cfg.num_kv_heads, world)[rank]
-    hkv_l = hi - lo
-    hq_l = hkv_l * cfg.group
-    B, bs, D, dt = len(lens), cfg.block_size, cfg.head_dim, cfg.dtype
-    n_new = [1] * B if n_new is None else list(n_new)
-    T = sum(n_new)
-    blocks = sum(-(-n // bs) for n in lens) + 64
-    pool = PagedKVPool(blocks, bs, hkv_l, D, num_layers=1, dtype=dt, device=device,
-                       max_seqs=B, max_blocks_per_seq=max(-(-n // bs) for n in lens) + 1)
-    pool.shuffle_free_stack(1234 + seed)
-    pool.reserve(list(range(B)), list(lens))
-    g = torch.Generator(device=device).manual_seed(4321 + rank)
-    for t in (pool.k, pool.v):  # fill the whole pool: every block holds N(0,1)*scale data
-        t.normal_(0.0, cfg.value_scale, generator=g) if dt == torch.float32 else \
-            t.copy_(torch.randn(t.shape, generator=g, device=device).mul_(cfg.value_scale).to(dt))
-    q = (torch.randn((T, hq_l, D), generator=g, device=device) * cfg.value_scale).to(dt).float()
-    kn = (torch.randn((T, hkv_l, D), generator=g, device=device) * cfg.value_scale).to(dt)
-    vn = (torch.randn((T, hkv_l, D), generator=g, device=device) * cfg.value_scale).to(dt)
-    max_q = max(n_new)
-    # the configuration's split at N=1; with fewer KV heads per GPU the
-    # library's own choice keeps the CTA waves full
-    pt = cfg.partition_tokens if world == 1 else 0
-    pt = _lib.decode_partition_tokens(B, T, max_q, max(lens), hq_l, hkv_l, D, bs, dt, torch.float32, pt)
-    offs, ctx = [0], []
-    for n, k in zip(lens, n_new):
-        offs.append(offs[-1] + k)
-        ctx += list(range(n - k + 1, n + 1))
-    meta = torch.tensor(list(range(B)) + offs + ctx, dtype=torch.int32, device=device)
-    rows, offs_d, ctx_d = meta[:B], meta[B:2 * B + 1], meta[2 * B + 1:]
-    out = torch.empty_like(q)
-    if gather is not None:
-        nbytes = _lib.decode_gather_workspace_bytes(B, T, max_q, max(lens), hq_l, hkv_l, D, bs, dt,
-                                                    q.dtype, pt)
-    else:
-        nbytes = _lib.decode_workspace_bytes(B, T, max_q, max(lens), hq_l, hkv_l, D, bs, dt, q.dtype, pt)
-    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
-    common = dict(max_queries_per_seq=max_q, max_ctx_len=max(lens), score_scale=cfg.score_scale,
-                  seq_rows=rows, partition_tokens=pt, workspace=ws, status=pool.status)
-
-    def decode_only():
-        _lib.paged_decode(out, q, pool.k[0], pool.v[0], pool.tables, offs_d, ctx_d, **common)
-
-    def step():
-        if gather is not None:
-            # fused append + decode, then reduce with the all-gather fused in
-            _lib.decode_step_gather(q, pool.k[0], pool.v[0], kn, vn, pool.tables, offs_d, ctx_d,
-                                    gather, **common)
-            return
-        # append each row's new token at position ctx-1 and attend (fused)
-        _lib.decode_step(out, q, pool.k[0], pool.v[0], kn, vn, pool.tables, offs_d, ctx_d, **common)
-
-    return dict(pool=pool, q=q, out=out, step=step, decode_only=decode_only, hkv_local=hkv_l,
-                hq_local=hq_l, kv_range=(lo, hi), partition_tokens=pt, workspace_bytes=nbytes,
-                rows=T, max_q=max_q)
+    from cloverinfer_b200.workloads import build_decode_step
+    return build_decode_step(cfg, rank, world, lens, device, seed=seed, gather=gather, n_new=n_new)
 
 
 def run_b200(args):
