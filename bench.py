@@ -3,13 +3,16 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3] [--impl b200|reference]
 
 Under torchrun (N > 1) each rank owns Hkv/N KV heads (head sharding) and the
-step ends with an NCCL all-gather of the per-rank outputs.
+step ends with the all-gather of the per-rank outputs, fused into the split-K
+reduce over NVLink (``--gather nccl``: one NCCL all-gather instead).
 
 One "step" = one attention step of one layer for the whole batch at the
 configuration's context length: KV append of each sequence's new token fused
-with the paged decode (split-K) -> split-K reduce (-> all-gather).  ``value`` times that
-step on device-resident inputs (a CUDA graph replayed K times between CUDA
-events, max over ranks); ``e2e`` times the same step through the public
+with the paged decode (split-K) -> split-K reduce (-> all-gather).  ``value`` times K
+such steps on device-resident inputs, captured back to back in one CUDA graph
+as consecutive layers run (each step waits for the previous one: they share
+the split-K workspace), between CUDA events, max over ranks; W warm-up steps
+run the same way before.  ``e2e`` times the same step through the public
 ``B200AttentionBackend.decode_layer_batch`` API with host (pinned) inputs and
 outputs, as the attention node calls it.  The metric is algorithmic KV bytes
 read per step (sum_s ctx_s * Hkv * D * 2 * elem) / step time, whole job.
@@ -247,16 +250,29 @@ def run_b200(args):
         for _ in range(3):  # eager warm-up (module load, tensor maps, NCCL comm init)
             full_step()
     torch.cuda.synchronize(device)
+    # K timed steps back to back in one CUDA graph: one graph launch per K
+    # steps, and programmatic dependent launch between a step's reduce and the
+    # next step's decode.  The warm-up replays the same graph (its first launch
+    # also uploads it), so at least W steps run untimed.
     graph = None
     if not args.no_graph:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
-            full_step()
-    run = graph.replay if graph is not None else full_step
+            for _ in range(args.steps):
+                full_step()
+    warm_replays = -(-args.warmup // args.steps)
+    warm_steps = warm_replays * args.steps if graph is not None else args.warmup
+
+    def run_steps(n):
+        if graph is not None:
+            graph.replay()
+        else:
+            for _ in range(n):
+                full_step()
 
     with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            run()
+        for _ in range(warm_replays if graph is not None else 1):
+            run_steps(args.warmup)
     torch.cuda.synchronize(device)
     st["pool"].check_status()
 
@@ -270,8 +286,7 @@ def run_b200(args):
     e1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         e0.record(stream)
-        for _ in range(args.steps):
-            run()
+        run_steps(args.steps)
         e1.record(stream)
     torch.cuda.synchronize(device)
     _barrier(world)
@@ -302,7 +317,7 @@ def run_b200(args):
     if graph is not None:
         graph.reset()
     dec_graph.reset()
-    del run, graph, dec_graph
+    del graph, dec_graph
     torch.cuda.synchronize(device)
 
     # ---------------- e2e through the public API (host buffers in, host out)
@@ -322,7 +337,8 @@ def run_b200(args):
                    "head_dim": cfg.head_dim, "block_size": cfg.block_size,
                    "partition_tokens": st["partition_tokens"],
                    "parallelism": f"kv-head-shard{world}", "gather": gather_kind,
-                   "cuda_graph": used_graph,
+                   "cuda_graph": ("%d steps per graph" % args.steps) if used_graph else "none",
+                   "warmup_steps_run": warm_steps,
                    "l2": "inputs > L2 (KV %.0f MB per GPU)" % (local_kv / 1e6)},
         "steps_per_s": round(1e3 / ms, 2),
         "tokens_per_s": round(T * 1e3 / ms, 2),

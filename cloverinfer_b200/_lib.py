@@ -30,6 +30,8 @@ DEV_OOM = 0x8
 DEV_TIMEOUT = 0x10
 DEV_CTX_RANGE = 0x20
 
+PARTITION_BALANCED = -1  # CLOVER_B200_PARTITION_BALANCED: the balanced split
+
 F32, F16, BF16 = 0, 1, 2
 _DTYPE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 
@@ -199,6 +201,7 @@ def decode_workspace_bytes(n_seqs, n_rows, max_queries_per_seq, max_ctx_len, num
 def decode_partition_tokens(n_seqs, n_rows, max_queries_per_seq, max_ctx_len, num_q_heads,
                             num_kv_heads, head_dim, block_size, kv_dtype, q_dtype,
                             partition_tokens=0) -> int:
+    """Partition length the call would use; 0 for the balanced split."""
     pt = int(lib().clover_b200_decode_partition_tokens(
         n_seqs, n_rows, max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads, head_dim,
         block_size, dtype_code(kv_dtype), dtype_code(q_dtype), partition_tokens))

@@ -37,120 +37,10 @@
 
 #include <cudaTypedefs.h>
 
-#include "common.cuh"
+#include "decode_common.cuh"
 
 namespace clover {
 
-constexpr int kNumWarps = 4;  // SIMT path
-constexpr int kThreads = kNumWarps * 32;
-constexpr int kMmaCols = 8;
-
-// Tensor-core path launch shape (compile-time knobs).
-#ifndef CLOVER_MMA_WARPS
-#define CLOVER_MMA_WARPS 2
-#endif
-#ifndef CLOVER_MMA_STAGES
-#define CLOVER_MMA_STAGES 2
-#endif
-#ifndef CLOVER_MMA_STAGE_TOKENS
-#define CLOVER_MMA_STAGE_TOKENS 16
-#endif
-#ifndef CLOVER_MMA_MIN_CTAS
-#define CLOVER_MMA_MIN_CTAS 6
-#endif
-constexpr int kMmaWarps = CLOVER_MMA_WARPS;
-constexpr int kMmaThreads = kMmaWarps * 32;
-
-struct DecodeArgs {
-  void* out;
-  int64_t out_stride;
-  const void* q;
-  int64_t q_stride;
-  int32_t q_dtype;
-  const void* k_cache;
-  const void* v_cache;
-  const int32_t* tables;
-  int32_t table_stride;
-  const int32_t* seq_rows;
-  const int32_t* qsl;
-  const int32_t* ctx;
-  int32_t num_q_heads;
-  int32_t num_kv_heads;
-  int32_t group;
-  int32_t block_size;
-  int64_t num_blocks;
-  float scale_log2;
-  int32_t part_tokens;
-  int32_t max_parts;
-  int32_t cols_per_cta;
-  int32_t col_chunks;
-  float* part_out;
-  float* part_lse;
-  int32_t* status;
-  // Fused KV append (decode_step): row r's new token k_new/v_new[r] (all local
-  // KV heads, token stride new_stride elements) is written to position
-  // ctx[r] - 1 before attending.  Null when the caller appended already.
-  const void* k_new;
-  const void* v_new;
-  int64_t new_stride;
-  int32_t kv_esz;
-  // Gathered output (decode_step_gather): every row goes through the split-K
-  // workspace, even a single-partition one, and the reduce writes the output.
-  int32_t force_split;
-};
-
-// Fused output all-gather over peer memory, LL style: every value travels as
-// one 8-byte word (epoch << 32 | fp32 bits) written with a single 64-bit
-// store, so a reader that sees the current epoch in a word also sees its
-// value — no fences and no global barrier.  Words live in each rank's receive
-// buffer, [2 parities][rows, total_q_heads, D] (parity = epoch & 1).  The
-// local sync words: kSyncDone counts finished reduce CTAs of this launch;
-// kSyncEpoch is the number of completed calls.
-constexpr int kSyncDone = 0;
-constexpr int kSyncEpoch = 1;
-constexpr int kSyncInts = 64;
-
-struct GatherArgs {
-  uint64_t* const* peer_ll;  // [n_ranks] receive buffers (own one at [rank])
-  int32_t* sync;             // this rank's sync words
-  int32_t n_ranks, rank, q_head_offset, total_q_heads;
-  int64_t ll_half_words;     // words per parity half (>= rows * total_q_heads * D)
-  int32_t units;             // rows * local heads * 32-dim chunks
-};
-
-struct ColInfo {
-  int32_t qrow, qhead, limit;
-  bool valid;
-};
-
-__device__ __forceinline__ ColInfo col_info(const DecodeArgs& a, int row0, int nq, int kvh,
-                                            int cglob) {
-  ColInfo c{0, 0, 0, false};
-  if (cglob < nq * a.group) {
-    const int j = cglob / a.group;
-    c.qrow = row0 + j;
-    c.qhead = kvh * a.group + (cglob - j * a.group);
-    c.limit = __ldg(a.ctx + c.qrow);
-    c.valid = true;
-  }
-  return c;
-}
-
-__device__ __forceinline__ float load_q(const DecodeArgs& a, int64_t idx) {
-  switch (a.q_dtype) {
-    case CLOVER_B200_F32: return __ldg(static_cast<const float*>(a.q) + idx);
-    case CLOVER_B200_F16: return __half2float(static_cast<const __half*>(a.q)[idx]);
-    default: return __bfloat162float(static_cast<const __nv_bfloat16*>(a.q)[idx]);
-  }
-}
-
-__device__ __forceinline__ void store_out(const DecodeArgs& a, int64_t idx, float v) {
-  switch (a.q_dtype) {
-    case CLOVER_B200_F32: static_cast<float*>(a.out)[idx] = v; break;
-    case CLOVER_B200_F16: static_cast<__half*>(a.out)[idx] = __float2half_rn(v); break;
-    default: static_cast<__nv_bfloat16*>(a.out)[idx] = __float2bfloat16_rn(v); break;
-  }
-}
 
 // Common CTA prologue: the token range this CTA owns.  Returns false if the
 // CTA has no work.
@@ -305,45 +195,17 @@ __device__ __forceinline__ void merge_store_rt(const DecodeArgs& a, const CtaWor
   }
 }
 
-// ------------------------------------------------------------------ tensor-core path
-// One pipeline stage holds BPS consecutive KV blocks (K and V tiles) of one KV
-// head: kTok = BPS * BS token rows of D bf16/fp16 values, stored per 64-column
-// chunk as 128-byte rows with the TMA 128-byte swizzle.
-template <int D, int BS>
-struct MmaGeom {
-  static constexpr int kChunks = D / 64;  // 128-byte swizzle atoms per row
-  static constexpr int kBps = (CLOVER_MMA_STAGE_TOKENS > BS ? CLOVER_MMA_STAGE_TOKENS : BS) / BS;
-  static constexpr int kTok = kBps * BS;   // tokens per stage
-  static constexpr int kTile = kTok * D * 2;
-  static constexpr int kStage = 2 * kTile;  // K + V
-  // keep the ring within the per-CTA shared memory limit
-  static constexpr int kStages = kMmaWarps * CLOVER_MMA_STAGES * kStage <= 200 * 1024
-                                     ? CLOVER_MMA_STAGES
-                                     : (kMmaWarps * 2 * kStage <= 200 * 1024 ? 2 : 1);
-  static constexpr int kPipeBytes = kMmaWarps * kStages * kStage;
-  static constexpr int kRedBytes = kMmaWarps * kMmaCols * (D + 4) * 4 + 2 * kMmaWarps * kMmaCols * 4;
-  static constexpr int kSmem = (kPipeBytes > kRedBytes ? kPipeBytes : kRedBytes) + 1024;
-  static constexpr int kMaxGroupsPerWarp = 32;  // one lane holds the block ids of one group
-};
 
-// byte offset of 16-byte chunk `cg` (along head_dim) of stage row `r`
-template <int TOK>
-__device__ __forceinline__ uint32_t swz(int r, int cg) {
-  const int c64 = cg >> 3, c = cg & 7;
-  return (uint32_t)(c64 * TOK * 128 + r * 128 + ((c ^ (r & 7)) << 4));
-}
-
-template <typename T, bool QF32, int D, int BS>
-__global__ void __launch_bounds__(kMmaThreads, D >= 256 ? 1 : CLOVER_MMA_MIN_CTAS)
+template <typename T, bool QF32, int D, int BS, int NT>
+__global__ void __launch_bounds__(kMmaThreads, mma_min_ctas<D, NT>())
 paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const DecodeArgs a) {
-  using G = MmaGeom<D, BS>;
+  using G = MmaGeom<D, BS, NT>;
   constexpr int NW = kMmaWarps;
   constexpr int STAGES = G::kStages;
   constexpr int BPS = G::kBps;
   constexpr int TOK = G::kTok;
-  constexpr int MT = TOK / 16;  // token m-tiles per stage
-  constexpr int KK = D / 16;    // k-steps (QK) / m-tiles (PV) over head_dim
+  constexpr int KK = D / 16;  // k-steps (QK) / m-tiles (PV) over head_dim
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bars[NW * STAGES];
   __shared__ int s_abort;
@@ -422,39 +284,11 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
     }
   };
 
-  // Query fragments (MMA B operand, columns = lane / 4).
-  uint32_t qh[KK][2], ql[KK][2];
-  {
-    const ColInfo ci = col_info(a, w.row0, w.nq, w.kvh, w.chunk * kMmaCols + (lane >> 2));
-    const int64_t qbase = (int64_t)ci.qrow * a.q_stride + (int64_t)ci.qhead * D;
-#pragma unroll
-    for (int kk = 0; kk < KK; ++kk) {
-      const int d0 = kk * 16 + (lane & 3) * 2;
-      float x0 = 0.f, x1 = 0.f, x8 = 0.f, x9 = 0.f;
-      if (ci.valid) {
-        x0 = load_q(a, qbase + d0);
-        x1 = load_q(a, qbase + d0 + 1);
-        x8 = load_q(a, qbase + d0 + 8);
-        x9 = load_q(a, qbase + d0 + 9);
-      }
-      if (QF32) {
-        split_pack<T>(x0, x1, qh[kk][0], ql[kk][0]);
-        split_pack<T>(x8, x9, qh[kk][1], ql[kk][1]);
-      } else {
-        qh[kk][0] = Pack<T>::pack(x0, x1);
-        qh[kk][1] = Pack<T>::pack(x8, x9);
-      }
-    }
-  }
-  // Causal limits of this thread's two accumulator columns.
-  const int ca = (lane & 3) * 2;
-  int lim_a, lim_b;
-  {
-    const ColInfo c0 = col_info(a, w.row0, w.nq, w.kvh, w.chunk * kMmaCols + ca);
-    const ColInfo c1 = col_info(a, w.row0, w.nq, w.kvh, w.chunk * kMmaCols + ca + 1);
-    lim_a = c0.valid ? c0.limit : 0;
-    lim_b = c1.valid ? c1.limit : 0;
-  }
+  // Query fragments (MMA B operand, columns = lane / 4 of each n-tile) and
+  // the causal limits of this thread's accumulator columns.
+  MmaCols<D, NT> c;
+  load_cols<T, QF32, D, NT>(a, w.row0, w.nq, w.kvh, w.chunk * G::kCols, c, lane);
+  c.reset();
 
   // First stages: issued once the query and block-id loads are both in
   // flight, so their latencies overlap.
@@ -463,10 +297,6 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   int issued = npre;
   int consumed = 0;
 
-  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
-  float acc[KK][4];
-#pragma unroll
-  for (int i = 0; i < KK; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   bool timed_out = false;
 
   for (int k = 0; k < n_mine; ++k) {
@@ -479,98 +309,8 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
     const uint32_t ks = ring + s * G::kStage;
     const uint32_t vs = ks + G::kTile;
     const int tok0 = w.tok_begin + (warp + k * NW) * TOK;
-    const int nvalid = w.tok_end - tok0;
-    if (nvalid < TOK) {
-      // Rows past the end of the context (stale data, or blocks not fetched)
-      // are zeroed in V so that P = 0 never multiplies a non-finite value.
-      uint8_t* vg = smem + (vs - smem_addr(smem));
-      for (int idx = lane; idx < (TOK - nvalid) * (D / 8); idx += 32) {
-        const int r = nvalid + idx / (D / 8);
-        *reinterpret_cast<uint4*>(vg + swz<TOK>(r, idx % (D / 8))) = make_uint4(0, 0, 0, 0);
-      }
-      __syncwarp();
-    }
-
-    // ---- S = K . Q^T (tokens x columns): independent accumulator chains
-    // (even/odd k-steps, hi/lo query halves) summed at the end.
-    float sc[MT][4];
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-      float ch[QF32 ? 4 : 2][4];
-#pragma unroll
-      for (int c = 0; c < (QF32 ? 4 : 2); ++c) ch[c][0] = ch[c][1] = ch[c][2] = ch[c][3] = 0.f;
-      const int r = mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-#pragma unroll
-      for (int kk = 0; kk < KK; ++kk) {
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4(ks + swz<TOK>(r, kk * 2 + (lane >> 4)), a0, a1, a2, a3);
-        MmaOp<T>::run(ch[kk & 1], a0, a1, a2, a3, qh[kk][0], qh[kk][1]);
-        if (QF32) MmaOp<T>::run(ch[2 + (kk & 1)], a0, a1, a2, a3, ql[kk][0], ql[kk][1]);
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        sc[mt][e] = QF32 ? (ch[0][e] + ch[1][e]) + (ch[2][e] + ch[3][e]) : ch[0][e] + ch[1][e];
-    }
-    // ---- scale (base-2 domain), causal mask, stage max per column
-    float mx_a = -INFINITY, mx_b = -INFINITY;
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int t = tok0 + mt * 16 + (lane >> 2) + h * 8;
-        const float sa = t < lim_a ? sc[mt][2 * h] * a.scale_log2 : -INFINITY;
-        const float sb = t < lim_b ? sc[mt][2 * h + 1] * a.scale_log2 : -INFINITY;
-        sc[mt][2 * h] = sa;
-        sc[mt][2 * h + 1] = sb;
-        mx_a = fmaxf(mx_a, sa);
-        mx_b = fmaxf(mx_b, sb);
-      }
-    }
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-      mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, off));
-      mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, off));
-    }
-    const float nm_a = fmaxf(m_a, mx_a), nm_b = fmaxf(m_b, mx_b);
-    const float u_a = nm_a == -INFINITY ? 0.f : nm_a;
-    const float u_b = nm_b == -INFINITY ? 0.f : nm_b;
-    const float al_a = fast_exp2(m_a - u_a), al_b = fast_exp2(m_b - u_b);
-    m_a = nm_a;
-    m_b = nm_b;
-    l_a *= al_a;
-    l_b *= al_b;
-#pragma unroll
-    for (int i = 0; i < KK; ++i) {
-      acc[i][0] *= al_a;
-      acc[i][1] *= al_b;
-      acc[i][2] *= al_a;
-      acc[i][3] *= al_b;
-    }
-    // ---- O^T += V^T . P^T  (P split hi + lo; V^T via ldmatrix.trans)
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-      const float p0 = fast_exp2(sc[mt][0] - u_a), p1 = fast_exp2(sc[mt][1] - u_b);
-      const float p2 = fast_exp2(sc[mt][2] - u_a), p3 = fast_exp2(sc[mt][3] - u_b);
-      l_a += p0 + p2;
-      l_b += p1 + p3;
-      uint32_t h_top, l_top, h_bot, l_bot;
-      split_pack<T>(p0, p1, h_top, l_top);
-      split_pack<T>(p2, p3, h_bot, l_bot);
-      const uint32_t bh0 = movm_trans(h_top), bh1 = movm_trans(h_bot);
-      const uint32_t bl0 = movm_trans(l_top), bl1 = movm_trans(l_bot);
-      const int grp = lane >> 3;
-      const int r = mt * 16 + (lane & 7) + (grp >> 1) * 8;
-      uint32_t va[KK][4];
-#pragma unroll
-      for (int dm = 0; dm < KK; ++dm)
-        ldsm_x4_trans(vs + swz<TOK>(r, dm * 2 + (grp & 1)), va[dm][0], va[dm][1], va[dm][2], va[dm][3]);
-#pragma unroll
-      for (int dm = 0; dm < KK; ++dm)
-        MmaOp<T>::run(acc[dm], va[dm][0], va[dm][1], va[dm][2], va[dm][3], bh0, bh1);
-#pragma unroll
-      for (int dm = 0; dm < KK; ++dm)
-        MmaOp<T>::run(acc[dm], va[dm][0], va[dm][1], va[dm][2], va[dm][3], bl0, bl1);
-    }
+    mma_stage<T, QF32, D, TOK, NT>(ks, vs, smem + (vs - smem_addr(smem)), tok0,
+                                   w.tok_end - tok0, a.scale_log2, c, lane);
     __syncwarp();
     if (k + STAGES < n_mine) {
       issue(k + STAGES);
@@ -588,38 +328,46 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
     }
   }
 #pragma unroll
-  for (int off = 4; off < 32; off <<= 1) {
-    l_a += __shfl_xor_sync(0xffffffffu, l_a, off);
-    l_b += __shfl_xor_sync(0xffffffffu, l_b, off);
-  }
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      c.l[nt][0] += __shfl_xor_sync(0xffffffffu, c.l[nt][0], off);
+      c.l[nt][1] += __shfl_xor_sync(0xffffffffu, c.l[nt][1], off);
+    }
   __syncthreads();  // every warp is done with its ring: reuse it for the merge
   if (s_abort) {
     pdl_trigger();
     return;
   }
 
+  constexpr int COLS = G::kCols;
   float* red_acc = reinterpret_cast<float*>(smem);
-  float* red_m = red_acc + NW * kMmaCols * (D + 4);
-  float* red_l = red_m + NW * kMmaCols;
+  float* red_m = red_acc + NW * COLS * (D + 4);
+  float* red_l = red_m + NW * COLS;
   {
-    float* base = red_acc + (warp * kMmaCols) * (D + 4);
+    float* base = red_acc + (warp * COLS) * (D + 4);
+    const int ca = (lane & 3) * 2;
 #pragma unroll
-    for (int dm = 0; dm < KK; ++dm) {
-      const int d = dm * 16 + (lane >> 2);
-      base[ca * (D + 4) + d] = acc[dm][0];
-      base[(ca + 1) * (D + 4) + d] = acc[dm][1];
-      base[ca * (D + 4) + d + 8] = acc[dm][2];
-      base[(ca + 1) * (D + 4) + d + 8] = acc[dm][3];
-    }
-    if (lane < 4) {
-      red_m[warp * kMmaCols + ca] = m_a;
-      red_m[warp * kMmaCols + ca + 1] = m_b;
-      red_l[warp * kMmaCols + ca] = l_a;
-      red_l[warp * kMmaCols + ca + 1] = l_b;
+    for (int nt = 0; nt < NT; ++nt) {
+      const int cc = nt * kMmaCols + ca;
+#pragma unroll
+      for (int dm = 0; dm < KK; ++dm) {
+        const int d = dm * 16 + (lane >> 2);
+        base[cc * (D + 4) + d] = c.acc[nt][dm][0];
+        base[(cc + 1) * (D + 4) + d] = c.acc[nt][dm][1];
+        base[cc * (D + 4) + d + 8] = c.acc[nt][dm][2];
+        base[(cc + 1) * (D + 4) + d + 8] = c.acc[nt][dm][3];
+      }
+      if (lane < 4) {
+        red_m[warp * COLS + cc] = c.m[nt][0];
+        red_m[warp * COLS + cc + 1] = c.m[nt][1];
+        red_l[warp * COLS + cc] = c.l[nt][0];
+        red_l[warp * COLS + cc + 1] = c.l[nt][1];
+      }
     }
   }
   __syncthreads();
-  merge_store_rt(a, w, red_acc, red_m, red_l, kMmaCols, D, NW);
+  merge_store_rt(a, w, red_acc, red_m, red_l, COLS, D, NW);
   pdl_trigger();  // the split-K reduce may launch once every CTA got here
 }
 
@@ -730,13 +478,20 @@ constexpr int kReduceDims = 32;
 // result is valid in warp 0.
 constexpr int kPartsPerWarp = 16;
 
+// Partials of (query row r, head h): from the partition length for the
+// partition kernels, as recorded by the decode for the stream kernel; 0 for an
+// empty row.
+__device__ __forceinline__ int partial_count(const DecodeArgs& a, int r, int h, int lim) {
+  if (lim <= 0) return 0;
+  const int np = a.part_count != nullptr ? __ldcg(a.part_count + (int64_t)r * a.num_q_heads + h)
+                                         : (lim + a.part_tokens - 1) / a.part_tokens;
+  return np < a.max_parts ? np : a.max_parts;
+}
+
 __device__ __forceinline__ float reduce_unit(const DecodeArgs& a, int r, int h, int dim, int D,
-                                             float* s_m, float* s_l,
+                                             int npp, float* s_m, float* s_l,
                                              float (*s_o)[kReduceDims]) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int lim = __ldg(a.ctx + r);
-  const int np = lim > 0 ? (lim + a.part_tokens - 1) / a.part_tokens : 0;
-  const int npp = np < a.max_parts ? np : a.max_parts;
   const int64_t base = ((int64_t)r * a.num_q_heads + h) * a.max_parts;
   float m = -INFINITY, l = 0.f, o = 0.f;
   for (int p0 = 0; p0 < npp; p0 += kReduceWarps * kPartsPerWarp) {
@@ -798,10 +553,13 @@ splitk_reduce_kernel(const DecodeArgs a, int D) {
   const int r = blockIdx.x;
   const int h = blockIdx.y;
   const int lim = __ldg(a.ctx + r);
-  if ((lim + a.part_tokens - 1) / a.part_tokens <= 1) return;  // written by the decode kernel
+  const int npp = partial_count(a, r, h, lim);
+  // Single-partition rows were written by the decode kernel, and so were the
+  // empty rows of the partition kernels; the stream kernel leaves those here.
+  if (npp == 1 || (npp == 0 && a.part_count == nullptr)) return;
   const int lane = threadIdx.x & 31;
   const int dim = blockIdx.z * kReduceDims + lane;
-  const float v = reduce_unit(a, r, h, dim, D, s_m, s_l, s_o);
+  const float v = reduce_unit(a, r, h, dim, D, npp, s_m, s_l, s_o);
   if (threadIdx.x < 32 && dim < D) store_out(a, (int64_t)r * a.out_stride + (int64_t)h * D + dim, v);
 }
 
@@ -843,7 +601,8 @@ reduce_gather_kernel(const DecodeArgs a, const GatherArgs g, int D) {
     const int h = (u / dchunks) % heads;
     const int r = u / (dchunks * heads);
     const int dim = dc * kReduceDims + lane;
-    const float v = reduce_unit(a, r, h, dim, D, s_m, s_l, s_o);
+    const int npp = partial_count(a, r, h, __ldg(a.ctx + r));
+    const float v = reduce_unit(a, r, h, dim, D, npp, s_m, s_l, s_o);
     if (warp == 0 && dim < D) {
       const uint64_t word = ((uint64_t)(uint32_t)epoch << 32) | (uint64_t)__float_as_uint(v);
       const int64_t idx = half + ((int64_t)r * g.total_q_heads + g.q_head_offset + h) * D + dim;
@@ -989,45 +748,13 @@ static int choose_partition(int max_ctx, int BS, int rows_x_kvh, bool mma) {
   return pt;
 }
 
-// Programmatic dependent launch: on by default; CLOVER_B200_PDL=0 turns it off.
-static bool pdl_enabled() {
-  static const bool on = [] {
-    const char* e = getenv("CLOVER_B200_PDL");
-    return !(e && e[0] == '0');
-  }();
-  return on;
-}
 
-template <typename... KArgs, typename... Args>
-static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                              cudaStream_t s, Args&&... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
-}
-
-template <typename Kern>
-static int set_smem(Kern k, int bytes) {
-  static std::mutex mu;
-  std::lock_guard<std::mutex> lock(mu);
-  return check_cuda(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
-                    "cudaFuncSetAttribute");
-}
-
-template <typename T, bool QF32, int D, int BS>
+template <typename T, bool QF32, int D, int BS, int NT>
 static int launch_mma(const DecodeArgs& a, const CUtensorMap& tk, const CUtensorMap& tv,
                       dim3 grid, cudaStream_t s) {
-  using G = MmaGeom<D, BS>;
+  using G = MmaGeom<D, BS, NT>;
   static uint64_t configured = 0;  // one bit per device ordinal
-  auto kern = paged_decode_mma_kernel<T, QF32, D, BS>;
+  auto kern = paged_decode_mma_kernel<T, QF32, D, BS, NT>;
   int dev = 0;
   int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   if (rc) return rc;
@@ -1040,20 +767,26 @@ static int launch_mma(const DecodeArgs& a, const CUtensorMap& tk, const CUtensor
                     "paged_decode_mma launch");
 }
 
-template <typename T, bool QF32, int D>
+template <typename T, bool QF32, int D, int NT>
 static int dispatch_bs(int BS, const DecodeArgs& a, const CUtensorMap& tk, const CUtensorMap& tv,
                        dim3 grid, cudaStream_t s) {
-  return BS == 16 ? launch_mma<T, QF32, D, 16>(a, tk, tv, grid, s)
-                  : launch_mma<T, QF32, D, 32>(a, tk, tv, grid, s);
+  return BS == 16 ? launch_mma<T, QF32, D, 16, NT>(a, tk, tv, grid, s)
+                  : launch_mma<T, QF32, D, 32, NT>(a, tk, tv, grid, s);
 }
 
+// 16-column CTAs (two n-tiles) exist for head_dim 64 and 128.
 template <typename T, bool QF32>
 static int dispatch_d(int D, int BS, const DecodeArgs& a, const CUtensorMap& tk,
                       const CUtensorMap& tv, dim3 grid, cudaStream_t s) {
+  const bool wide = a.cols_per_cta > kMmaCols;
   switch (D) {
-    case 64: return dispatch_bs<T, QF32, 64>(BS, a, tk, tv, grid, s);
-    case 128: return dispatch_bs<T, QF32, 128>(BS, a, tk, tv, grid, s);
-    default: return dispatch_bs<T, QF32, 256>(BS, a, tk, tv, grid, s);
+    case 64:
+      return wide ? dispatch_bs<T, QF32, 64, 2>(BS, a, tk, tv, grid, s)
+                  : dispatch_bs<T, QF32, 64, 1>(BS, a, tk, tv, grid, s);
+    case 128:
+      return wide ? dispatch_bs<T, QF32, 128, 2>(BS, a, tk, tv, grid, s)
+                  : dispatch_bs<T, QF32, 128, 1>(BS, a, tk, tv, grid, s);
+    default: return dispatch_bs<T, QF32, 256, 1>(BS, a, tk, tv, grid, s);
   }
 }
 
@@ -1090,9 +823,12 @@ static int64_t workspace_bytes(int64_t rows, int64_t hq, int64_t D, int64_t part
 
 struct DecodePlan {
   bool mma;
+  bool stream;  // balanced decomposition (paged_decode_stream.cu)
   int cols_per_cta, col_chunks, part_tokens, max_parts;
-  int64_t workspace_bytes;
+  int64_t workspace_bytes;         // paged_decode / decode_step
+  int64_t gather_workspace_bytes;  // decode_step_gather (every row through the workspace)
 };
+
 
 // The launch shape of one paged_decode call; shared by the workspace query so
 // callers size the workspace for exactly what the launch will use.
@@ -1114,12 +850,15 @@ static int make_plan(int n_seqs, int n_rows, int max_q, int max_ctx, int hq, int
     return set_error(CLOVER_B200_ERR_UNSUPPORTED, "paged_decode: head_dim %d > 256", D);
   const int ncols_seq = max_q * group;
   if (pl->mma) {
-    pl->cols_per_cta = kMmaCols;
+    // two n-tiles when a sequence has more than 8 columns (multi-token GQA
+    // rows): every KV block is then read once for up to 16 columns
+    pl->cols_per_cta = ncols_seq > kMmaCols && D <= 128 ? 2 * kMmaCols : kMmaCols;
   } else {
     pl->cols_per_cta = ncols_seq >= 8 ? 8 : ncols_seq >= 4 ? 4 : ncols_seq >= 2 ? 2 : 1;
   }
   pl->col_chunks = (ncols_seq + pl->cols_per_cta - 1) / pl->cols_per_cta;
   int pt = partition_tokens;
+  const bool want_stream = partition_tokens == CLOVER_B200_PARTITION_BALANCED;
   if (pt <= 0) {
     pt = choose_partition(max_ctx, BS, n_seqs * hkv * pl->col_chunks, pl->mma);
   } else {
@@ -1131,11 +870,37 @@ static int make_plan(int n_seqs, int n_rows, int max_q, int max_ctx, int hq, int
   }
   pl->part_tokens = pt;
   pl->max_parts = max_ctx > 0 ? (max_ctx + pt - 1) / pt : 1;
+  pl->stream = false;
+  if (want_stream && pl->mma && MmaGeomBps(BS) == 1 && n_seqs <= kStreamMaxSeqs) {
+    // Stream decomposition: units of one block; a segment of n units spread
+    // over `per`-unit worker ranges has at most min(n, workers / segments
+    // per sequence + 1) parts.  Unit keys pack (segment << 16 | block).
+    const int64_t units = max_ctx > 0 ? ((int64_t)max_ctx + BS - 1) / BS : 1;
+    const int64_t hc = (int64_t)hkv * pl->col_chunks;
+    int grid = 0;
+    if (units < 65536 && (int64_t)(n_seqs + 1) * hc < 32768 &&
+        (int64_t)n_seqs * hc * units < INT32_MAX &&
+        stream_decode(kv_dtype, q_dtype, D, BS, pl->cols_per_cta, nullptr, nullptr, nullptr, nullptr,
+                      &grid) ==
+            CLOVER_B200_OK &&
+        grid > 0) {
+      const int64_t workers = (int64_t)grid * kMmaWarps;
+      const int64_t bound = (workers + hc - 1) / hc + 1;
+      pl->stream = true;
+      pl->part_tokens = 0;
+      pl->max_parts = (int)(bound < units ? bound : units);
+      pl->workspace_bytes = split_workspace_bytes(n_rows, hq, D, pl->max_parts) +
+                            align256((int64_t)n_rows * hq * 4);
+      pl->gather_workspace_bytes = pl->workspace_bytes;
+      return CLOVER_B200_OK;
+    }
+  }
   if (pl->max_parts > kReduceMaxParts)
     return set_error(CLOVER_B200_ERR_UNSUPPORTED,
                      "paged_decode: %d partitions > %d (raise partition_tokens)", pl->max_parts,
                      kReduceMaxParts);
   pl->workspace_bytes = workspace_bytes(n_rows, hq, D, pl->max_parts);
+  pl->gather_workspace_bytes = split_workspace_bytes(n_rows, hq, D, pl->max_parts);
   return CLOVER_B200_OK;
 }
 
@@ -1198,8 +963,7 @@ static int decode_impl(
     if (num_blocks * (int64_t)block_size > INT32_MAX)
       return set_error(CLOVER_B200_ERR_UNSUPPORTED, "paged_decode: cache exceeds 2^31 slots");
   }
-  const int64_t need = gather ? split_workspace_bytes(n_query_rows, num_q_heads, head_dim, pl.max_parts)
-                              : pl.workspace_bytes;
+  const int64_t need = gather ? pl.gather_workspace_bytes : pl.workspace_bytes;
   if (need > 0 && (workspace == nullptr || workspace_bytes_ < need))
     return set_error(CLOVER_B200_ERR_WORKSPACE, "paged_decode: workspace needs %lld bytes",
                      (long long)need);
@@ -1244,6 +1008,22 @@ static int decode_impl(
   a.new_stride = new_token_stride;
   a.kv_esz = kv_dtype == CLOVER_B200_F32 ? 4 : 2;
   a.force_split = gather != nullptr;
+  a.n_seqs = n_seqs;
+  a.max_ctx = max_ctx_len;
+  a.max_q = max_queries_per_seq > 0 ? max_queries_per_seq : 1;
+  a.min_units = kStreamMinUnits;
+  a.part_count = nullptr;
+  if (pl.stream) {
+    // Stream workspace: partials, their log-sum-exp, then the part counts.
+    a.part_tokens = block_size;
+    a.part_out = static_cast<float*>(workspace);
+    a.part_lse = reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                          align256((int64_t)n_query_rows * num_q_heads *
+                                                   max_parts * head_dim * 4));
+    a.part_count = reinterpret_cast<int32_t*>(
+        static_cast<char*>(workspace) +
+        split_workspace_bytes(n_query_rows, num_q_heads, head_dim, max_parts));
+  }
 
   cudaStream_t s = (cudaStream_t)stream;
   if (k_new != nullptr) {
@@ -1268,7 +1048,15 @@ static int decode_impl(
     }
   }
   const dim3 grid(max_parts, num_kv_heads * col_chunks, n_seqs);
-  if (mma) {
+  if (pl.stream) {
+    CUtensorMap tk, tv;
+    rc = get_tmap(k_cache, kv_dtype, head_dim, num_kv_heads, block_size, num_blocks, &tk);
+    if (rc) return rc;
+    rc = get_tmap(v_cache, kv_dtype, head_dim, num_kv_heads, block_size, num_blocks, &tv);
+    if (rc) return rc;
+    rc = stream_decode(kv_dtype, q_dtype, head_dim, block_size, cols_per_cta, &a, &tk, &tv, s,
+                       nullptr);
+  } else if (mma) {
     CUtensorMap tk, tv;
     rc = get_tmap(k_cache, kv_dtype, head_dim, num_kv_heads, block_size, num_blocks, &tk);
     if (rc) return rc;
@@ -1303,9 +1091,10 @@ static int decode_impl(
                                  a, g, head_dim),
                       "reduce_gather launch");
   }
-  if (max_parts > 1) {
+  if (max_parts > 1 || pl.stream) {
     // Rows with several partitions are combined here; single-partition rows
-    // were written by the decode kernel and return at once.
+    // were written by the decode kernel and return at once (the stream
+    // kernel also leaves the empty rows' zeros to this kernel).
     const dim3 rgrid(n_query_rows, num_q_heads, (head_dim + kReduceDims - 1) / kReduceDims);
     rc = check_cuda(launch_pdl(splitk_reduce_kernel, rgrid, dim3(kReduceWarps * 32), 0, s, a,
                                head_dim),
@@ -1358,7 +1147,7 @@ extern "C" int64_t clover_b200_decode_gather_workspace_bytes(
   if (make_plan(n_seqs, n_query_rows, max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads,
                 head_dim, block_size, kv_dtype, q_dtype, partition_tokens, &pl) != CLOVER_B200_OK)
     return -1;
-  return split_workspace_bytes(n_query_rows, num_q_heads, head_dim, pl.max_parts);
+  return pl.gather_workspace_bytes;
 }
 
 extern "C" int64_t clover_b200_gather_sync_bytes(void) { return (int64_t)kSyncInts * 4; }

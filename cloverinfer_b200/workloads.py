@@ -98,10 +98,13 @@ def kv_bytes(ctx_per_seq: List[int], num_kv_heads: int, head_dim: int, dtype: to
     return sum(ctx_per_seq) * num_kv_heads * head_dim * 2 * e
 
 
-def build_decode_step(cfg, rank, world, lens, device, seed=0, gather=None, n_new=None):
+def build_decode_step(cfg, rank, world, lens, device, seed=0, gather=None, n_new=None,
+                      partition_tokens=0):
     """Pool + static buffers for one decode step: sequence b holds lens[b]
     tokens after the step, n_new[b] of them (default 1) appended by it and
-    attended causally."""
+    attended causally.  ``partition_tokens``: 0 leaves the split to the
+    library, -1 asks for the balanced split, None takes the configuration's
+    fixed partition length on one GPU (the library's choice on several)."""
     from . import _lib
     from .head_groups import kv_head_shards
     from .kv_cache import PagedKVPool
@@ -125,10 +128,12 @@ def build_decode_step(cfg, rank, world, lens, device, seed=0, gather=None, n_new
     kn = (torch.randn((T, hkv_l, D), generator=g, device=device) * cfg.value_scale).to(dt)
     vn = (torch.randn((T, hkv_l, D), generator=g, device=device) * cfg.value_scale).to(dt)
     max_q = max(n_new)
-    # the configuration's split at N=1; with fewer KV heads per GPU the
-    # library's own choice keeps the CTA waves full
-    pt = cfg.partition_tokens if world == 1 else 0
+    pt = partition_tokens
+    if pt is None:
+        pt = cfg.partition_tokens if world == 1 else 0
     pt = _lib.decode_partition_tokens(B, T, max_q, max(lens), hq_l, hkv_l, D, bs, dt, torch.float32, pt)
+    if pt == 0:
+        pt = _lib.PARTITION_BALANCED  # the library took the balanced split
     offs, ctx = [0], []
     for n, k in zip(lens, n_new):
         offs.append(offs[-1] + k)

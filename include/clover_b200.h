@@ -140,6 +140,16 @@ CLOVER_B200_API int clover_b200_kv_append(void* k_cache, void* v_cache, const vo
                           int64_t num_blocks, int32_t dtype, int32_t* dev_status, void* stream);
 
 /*
+ * partition_tokens = CLOVER_B200_PARTITION_BALANCED asks for the balanced
+ * split on the tensor-core path (bf16/fp16 cache, head_dim 64/128/256, block
+ * 16/32, at most 1024 sequences): the KV blocks of all sequences are divided
+ * evenly over every resident warp instead of into fixed-length partitions, so
+ * ragged batches launch no empty work.  Elsewhere it means the library's
+ * choice (as 0).
+ */
+#define CLOVER_B200_PARTITION_BALANCED (-1)
+
+/*
  * Bytes of split-K workspace clover_b200_paged_decode needs for a call with
  * the same sizes, dtypes and partition_tokens (0 = the library's choice);
  * 0 when every context fits one partition, -1 on invalid sizes.
@@ -152,8 +162,8 @@ CLOVER_B200_API int64_t clover_b200_decode_workspace_bytes(int32_t n_seqs, int32
 
 /*
  * The split-K partition length (tokens) clover_b200_paged_decode uses for a
- * call with these sizes (the library's choice when partition_tokens = 0), or
- * a negative error code.
+ * call with these sizes (the library's choice when partition_tokens = 0; 0
+ * for the balanced split), or a negative error code.
  */
 CLOVER_B200_API int clover_b200_decode_partition_tokens(int32_t n_seqs, int32_t n_query_rows,
                                            int32_t max_queries_per_seq, int32_t max_ctx_len,
