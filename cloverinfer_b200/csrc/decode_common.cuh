@@ -320,11 +320,19 @@ __device__ __forceinline__ void mma_stage(uint32_t ks, uint32_t vs, uint8_t* vge
   }
 }
 
-// Load the query fragments and causal limits of n-tile columns
-// [col0, col0 + 8 NT) of (query rows row0 .. row0 + nq - 1, KV head kvh).
-template <typename T, bool QF32, int D, int NT>
-__device__ __forceinline__ void load_cols(const DecodeArgs& a, int row0, int nq, int kvh, int col0,
-                                          MmaCols<D, NT>& c, int lane) {
+// Query values (fp32, as loaded) and causal limits of n-tile columns
+// [col0, col0 + 8 NT) of (query rows row0 .. row0 + nq - 1, KV head kvh):
+// the loads are issued here and first used by pack_cols, so other loads and
+// copies can be issued in between.
+template <int D, int NT>
+struct QRaw {
+  float x[NT][D / 16][4];
+  int lim[NT][2];
+};
+
+template <int D, int NT>
+__device__ __forceinline__ void load_cols_raw(const DecodeArgs& a, int row0, int nq, int kvh,
+                                              int col0, QRaw<D, NT>& r, int lane) {
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const ColInfo ci = col_info(a, row0, nq, kvh, col0 + nt * kMmaCols + (lane >> 2));
@@ -332,27 +340,46 @@ __device__ __forceinline__ void load_cols(const DecodeArgs& a, int row0, int nq,
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
       const int d0 = kk * 16 + (lane & 3) * 2;
-      float x0 = 0.f, x1 = 0.f, x8 = 0.f, x9 = 0.f;
-      if (ci.valid) {
-        x0 = load_q(a, qbase + d0);
-        x1 = load_q(a, qbase + d0 + 1);
-        x8 = load_q(a, qbase + d0 + 8);
-        x9 = load_q(a, qbase + d0 + 9);
-      }
-      if (QF32) {
-        split_pack<T>(x0, x1, c.qh[nt][kk][0], c.ql[nt][kk][0]);
-        split_pack<T>(x8, x9, c.qh[nt][kk][1], c.ql[nt][kk][1]);
-      } else {
-        c.qh[nt][kk][0] = Pack<T>::pack(x0, x1);
-        c.qh[nt][kk][1] = Pack<T>::pack(x8, x9);
-      }
+      r.x[nt][kk][0] = ci.valid ? load_q(a, qbase + d0) : 0.f;
+      r.x[nt][kk][1] = ci.valid ? load_q(a, qbase + d0 + 1) : 0.f;
+      r.x[nt][kk][2] = ci.valid ? load_q(a, qbase + d0 + 8) : 0.f;
+      r.x[nt][kk][3] = ci.valid ? load_q(a, qbase + d0 + 9) : 0.f;
     }
     const int ca = col0 + nt * kMmaCols + (lane & 3) * 2;
     const ColInfo c0 = col_info(a, row0, nq, kvh, ca);
     const ColInfo c1 = col_info(a, row0, nq, kvh, ca + 1);
-    c.lim[nt][0] = c0.valid ? c0.limit : 0;
-    c.lim[nt][1] = c1.valid ? c1.limit : 0;
+    r.lim[nt][0] = c0.valid ? c0.limit : 0;
+    r.lim[nt][1] = c1.valid ? c1.limit : 0;
   }
+}
+
+// MMA B-operand fragments (columns = lane / 4 of each n-tile) from the raw
+// query values: hi + lo 16-bit halves for fp32 queries.
+template <typename T, bool QF32, int D, int NT>
+__device__ __forceinline__ void pack_cols(const QRaw<D, NT>& r, MmaCols<D, NT>& c) {
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      if (QF32) {
+        split_pack<T>(r.x[nt][kk][0], r.x[nt][kk][1], c.qh[nt][kk][0], c.ql[nt][kk][0]);
+        split_pack<T>(r.x[nt][kk][2], r.x[nt][kk][3], c.qh[nt][kk][1], c.ql[nt][kk][1]);
+      } else {
+        c.qh[nt][kk][0] = Pack<T>::pack(r.x[nt][kk][0], r.x[nt][kk][1]);
+        c.qh[nt][kk][1] = Pack<T>::pack(r.x[nt][kk][2], r.x[nt][kk][3]);
+      }
+    }
+    c.lim[nt][0] = r.lim[nt][0];
+    c.lim[nt][1] = r.lim[nt][1];
+  }
+}
+
+template <typename T, bool QF32, int D, int NT>
+__device__ __forceinline__ void load_cols(const DecodeArgs& a, int row0, int nq, int kvh, int col0,
+                                          MmaCols<D, NT>& c, int lane) {
+  QRaw<D, NT> r;
+  load_cols_raw<D, NT>(a, row0, nq, kvh, col0, r, lane);
+  pack_cols<T, QF32, D, NT>(r, c);
 }
 
 // ------------------------------------------------------------------ host launch helpers

@@ -211,39 +211,76 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   __shared__ int s_abort;
 
   pdl_wait();  // inputs, tables and workspace are final before anything is read
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  // The prologue takes three dependent memory round trips before the first
+  // KV copy lands: (1) the sequence's rows and table row, (2) the rows'
+  // contexts and the block ids of the whole partition (ids past the context
+  // are loaded but never used), (3) the first copies, with the queries
+  // loaded alongside (an empty partition exits before loading them).
   CtaWork w;
-  if (!cta_work(a, w, D)) {
+  w.b = blockIdx.z;
+  w.p = blockIdx.x;
+  w.kvh = blockIdx.y / a.col_chunks;
+  w.chunk = blockIdx.y - w.kvh * a.col_chunks;
+  w.row0 = __ldg(a.qsl + w.b);
+  w.nq = __ldg(a.qsl + w.b + 1) - w.row0;
+  const int trow = a.seq_rows ? __ldg(a.seq_rows + w.b) : w.b;
+  // after a bounded wait gave up anywhere, later CTAs stop at once
+  const int stat = a.status != nullptr ? *(volatile int32_t*)a.status : 0;
+  w.tab = a.tables + (int64_t)trow * a.table_stride;
+  w.tok_begin = w.p * a.part_tokens;
+  const int c0 = w.chunk * G::kCols;
+  if ((stat & CLOVER_B200_DEV_TIMEOUT) || w.nq <= 0 || c0 >= w.nq * a.group) {
     pdl_trigger();
     return;
+  }
+  // lane j of warp w holds the BPS ids of the warp's j-th stage group
+  // (groups w, w+NW, ... of the partition)
+  const int blk0 = w.tok_begin / BS;
+  const int n_grp_full = (a.part_tokens / BS + BPS - 1) / BPS;
+  int my_blk[BPS];
+#pragma unroll
+  for (int i = 0; i < BPS; ++i) {
+    const int gi = (warp + lane * NW) * BPS + i;  // block index within the partition
+    const int bi = blk0 + gi;
+    my_blk[i] = (warp + lane * NW < n_grp_full && gi * BS < a.part_tokens && bi < a.table_stride)
+                    ? __ldg(w.tab + bi)
+                    : -1;
+  }
+  // the longest causal limit among this chunk's rows bounds the token range
+  const int j_lo = c0 / a.group;
+  const int j_hi = min(w.nq - 1, (c0 + G::kCols - 1) / a.group);
+  int ctx_end = 0;
+  for (int j = j_lo; j <= j_hi; ++j) ctx_end = max(ctx_end, __ldg(a.ctx + w.row0 + j));
+  if (ctx_end > a.max_parts * a.part_tokens) {
+    if (threadIdx.x == 0 && w.p == 0 && w.kvh == 0) raise_status(a.status, CLOVER_B200_DEV_CTX_RANGE);
+    ctx_end = a.max_parts * a.part_tokens;
+  }
+  if (w.tok_begin >= ctx_end) {
+    if (w.p == 0) zero_empty_columns(a, w, D);
+    pdl_trigger();
+    return;
+  }
+  w.tok_end = min(w.tok_begin + a.part_tokens, ctx_end);
+  const int n_blk = (w.tok_end - w.tok_begin + BS - 1) / BS;
+  const int n_grp = (n_blk + BPS - 1) / BPS;
+  const int n_mine = warp < n_grp ? (n_grp - warp + NW - 1) / NW : 0;
+#pragma unroll
+  for (int i = 0; i < BPS; ++i) {
+    const int gi = (warp + lane * NW) * BPS + i;
+    if (lane < n_mine && gi < n_blk) {
+      if (my_blk[i] < 0 || my_blk[i] >= a.num_blocks) {
+        raise_status(a.status, CLOVER_B200_DEV_BAD_BLOCK);
+        my_blk[i] = 0;  // keep the pipeline well-formed; the output is flagged invalid
+      }
+    } else {
+      my_blk[i] = -1;
+    }
   }
   if (a.k_new != nullptr && append_new_tokens(a, w, D)) fence_proxy_async_global();
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-
-  // Block ids of this CTA's partition, fetched before the barrier set-up so
-  // their latency overlaps it: lane j of warp w holds the BPS ids of the
-  // warp's j-th stage group (groups w, w+NW, ... of the partition).
-  const int blk0 = w.tok_begin / BS;
-  const int n_blk = (w.tok_end - w.tok_begin + BS - 1) / BS;
-  const int n_grp = (n_blk + BPS - 1) / BPS;
-  const int n_mine = warp < n_grp ? (n_grp - warp + NW - 1) / NW : 0;
-  int my_blk[BPS];
-#pragma unroll
-  for (int i = 0; i < BPS; ++i) {
-    my_blk[i] = -1;
-    const int gi = (warp + lane * NW) * BPS + i;  // block index within the partition
-    if (lane < n_mine && gi < n_blk) {
-      const int bi = blk0 + gi;
-      int id = bi < a.table_stride ? __ldg(w.tab + bi) : -1;
-      if (id < 0 || id >= a.num_blocks) {
-        raise_status(a.status, CLOVER_B200_DEV_BAD_BLOCK);
-        id = 0;  // keep the pipeline well-formed; the output is flagged invalid
-      }
-      my_blk[i] = id;
-    }
-  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NW * STAGES; ++i) mbar_init(smem_addr(&bars[i]), 1);
@@ -284,18 +321,15 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
     }
   };
 
-  // Query fragments (MMA B operand, columns = lane / 4 of each n-tile) and
-  // the causal limits of this thread's accumulator columns.
-  MmaCols<D, NT> c;
-  load_cols<T, QF32, D, NT>(a, w.row0, w.nq, w.kvh, w.chunk * G::kCols, c, lane);
-  c.reset();
-
-  // First stages: issued once the query and block-id loads are both in
-  // flight, so their latencies overlap.
+  // First stages in flight, then the query fragments (MMA B operand) and the
+  // causal limits of this thread's accumulator columns.
   const int npre = n_mine < STAGES ? n_mine : STAGES;
   for (int k = 0; k < npre; ++k) issue(k);
   int issued = npre;
   int consumed = 0;
+  MmaCols<D, NT> c;
+  load_cols<T, QF32, D, NT>(a, w.row0, w.nq, w.kvh, c0, c, lane);
+  c.reset();
 
   bool timed_out = false;
 
@@ -476,7 +510,8 @@ constexpr int kReduceDims = 32;
 // partitions), folding them into a running (max, sum, value); the four warps
 // are merged in shared memory.  Every thread of the CTA must call it; the
 // result is valid in warp 0.
-constexpr int kPartsPerWarp = 16;
+constexpr int kPartsPerWarp = 16;         // splitk_reduce_kernel (6 CTAs per SM)
+constexpr int kGatherPartsPerWarp = 32;   // reduce_gather_kernel (a small grid)
 
 // Partials of (query row r, head h): from the partition length for the
 // partition kernels, as recorded by the decode for the stream kernel; 0 for an
@@ -488,16 +523,17 @@ __device__ __forceinline__ int partial_count(const DecodeArgs& a, int r, int h, 
   return np < a.max_parts ? np : a.max_parts;
 }
 
+template <int PPW>
 __device__ __forceinline__ float reduce_unit(const DecodeArgs& a, int r, int h, int dim, int D,
                                              int npp, float* s_m, float* s_l,
                                              float (*s_o)[kReduceDims]) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t base = ((int64_t)r * a.num_q_heads + h) * a.max_parts;
   float m = -INFINITY, l = 0.f, o = 0.f;
-  for (int p0 = 0; p0 < npp; p0 += kReduceWarps * kPartsPerWarp) {
-    float lv[kPartsPerWarp], ov[kPartsPerWarp];
+  for (int p0 = 0; p0 < npp; p0 += kReduceWarps * PPW) {
+    float lv[PPW], ov[PPW];
 #pragma unroll
-    for (int i = 0; i < kPartsPerWarp; ++i) {
+    for (int i = 0; i < PPW; ++i) {
       const int p = p0 + warp + i * kReduceWarps;
       const bool ok = p < npp;
       lv[i] = ok ? __ldcg(a.part_lse + base + p) : -INFINITY;
@@ -505,13 +541,13 @@ __device__ __forceinline__ float reduce_unit(const DecodeArgs& a, int r, int h, 
     }
     float mm = m;
 #pragma unroll
-    for (int i = 0; i < kPartsPerWarp; ++i) mm = fmaxf(mm, lv[i]);
+    for (int i = 0; i < PPW; ++i) mm = fmaxf(mm, lv[i]);
     const float u = mm == -INFINITY ? 0.f : mm;
     const float sc = fast_exp2(m - u);
     l *= sc;
     o *= sc;
 #pragma unroll
-    for (int i = 0; i < kPartsPerWarp; ++i) {
+    for (int i = 0; i < PPW; ++i) {
       const float e = fast_exp2(lv[i] - u);
       l += e;
       o = fmaf(e, ov[i], o);
@@ -559,7 +595,7 @@ splitk_reduce_kernel(const DecodeArgs a, int D) {
   if (npp == 1 || (npp == 0 && a.part_count == nullptr)) return;
   const int lane = threadIdx.x & 31;
   const int dim = blockIdx.z * kReduceDims + lane;
-  const float v = reduce_unit(a, r, h, dim, D, npp, s_m, s_l, s_o);
+  const float v = reduce_unit<kPartsPerWarp>(a, r, h, dim, D, npp, s_m, s_l, s_o);
   if (threadIdx.x < 32 && dim < D) store_out(a, (int64_t)r * a.out_stride + (int64_t)h * D + dim, v);
 }
 
@@ -587,10 +623,12 @@ reduce_gather_kernel(const DecodeArgs a, const GatherArgs g, int D) {
   __shared__ float s_m[kReduceWarps], s_l[kReduceWarps];
   __shared__ float s_o[kReduceWarps][kReduceDims];
   __shared__ int s_last;
+  // The epoch word is written only by this kernel's previous launch, which
+  // completed before the decode it waits for began: read it while waiting.
+  const int epoch = *(volatile int32_t*)(g.sync + kSyncEpoch) + 1;
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int epoch = *(volatile int32_t*)(g.sync + kSyncEpoch) + 1;
   const int64_t half = (int64_t)(epoch & 1) * g.ll_half_words;
   const int dchunks = (D + kReduceDims - 1) / kReduceDims;
   const int heads = a.num_q_heads;
@@ -602,7 +640,7 @@ reduce_gather_kernel(const DecodeArgs a, const GatherArgs g, int D) {
     const int r = u / (dchunks * heads);
     const int dim = dc * kReduceDims + lane;
     const int npp = partial_count(a, r, h, __ldg(a.ctx + r));
-    const float v = reduce_unit(a, r, h, dim, D, npp, s_m, s_l, s_o);
+    const float v = reduce_unit<kGatherPartsPerWarp>(a, r, h, dim, D, npp, s_m, s_l, s_o);
     if (warp == 0 && dim < D) {
       const uint64_t word = ((uint64_t)(uint32_t)epoch << 32) | (uint64_t)__float_as_uint(v);
       const int64_t idx = half + ((int64_t)r * g.total_q_heads + g.q_head_offset + h) * D + dim;
