@@ -41,6 +41,14 @@ sys.path.insert(0, ROOT)
 
 METRIC = "paged decode-attn KV-read GB/s"
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one
+# paged_decode_mma_kernel launch from an ncu capture of the same workload and
+# kernel build: (config, GPUs) -> (bytes, summary file).
+NCU_TRAFFIC = {
+    ("c3", 1): (1.0740e9 + 8.032e6, "profiles/paged_decode_mma_c3_full.md"),
+    ("c3", 8): (134.363e6 + 3.985e6, "profiles/paged_decode_mma_c3_shard8_full.md"),
+}
+
 
 def _peaks():
     try:
@@ -344,7 +352,9 @@ def run_b200(args):
         "tokens_per_s": round(T * 1e3 / ms, 2),
         "pct_hbm_peak_per_gpu": round(100.0 * value / world / hbm_peak, 2),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(achieved / hbm_peak, 4), "traffic": None,
+                     "frac": round(achieved / hbm_peak, 4),
+                     "traffic": NCU_TRAFFIC.get((args.config, world), (None,))[0],
+                     "traffic_source": NCU_TRAFFIC.get((args.config, world), (None, None))[1],
                      "kernel": "paged_decode_mma_kernel + splitk_reduce_kernel",
                      "launch_ms": round(dec_ms, 5), "peak_kind": peak_kind},
         "clocks": clk,
