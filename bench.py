@@ -392,7 +392,7 @@ def run_e2e(cfg, lens, n_new, rank, world, device, args):
                                              for n in lens) + 64,
                               block_size=cfg.block_size, num_kv_heads=cfg.num_kv_heads, kv_dtype=dt,
                               device=device, max_seqs=B, shard=shard, shuffle_seed=77,
-                              partition_tokens=cfg.partition_tokens if world == 1 else 0,
+                              partition_tokens=0,
                               max_seq_len=max(lens) + 4 * steps_total + 4096, gather=args.gather,
                               max_rows_per_call=T)
     g = torch.Generator(device=device).manual_seed(99)

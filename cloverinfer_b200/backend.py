@@ -88,6 +88,23 @@ class _FastPlan:
         self.sizes = (ctypes.c_int64 * self.n)(*([self.qb] * B + [self.kb] * (2 * B) + [4 * n_meta]))
         self.srcs[self.n - 1] = ctypes.addressof(self.meta)
         self.out = torch.empty((B, hq_total, q_shape[-1]), dtype=out_dtype, pin_memory=True)
+        self.warm = False  # one eager call ran with this shape (one-time set-up done)
+        self.graphs: Dict[tuple, "_StepGraph"] = {}
+
+
+class _StepGraph:
+    """A captured fast-path step: H2D of the staging buffer, the fused
+    append + decode (+ reduce, + gather), D2H of the output and the status
+    word.  Owns the output and workspace its kernels were captured with."""
+
+    def __init__(self, graph, out_dev, workspace):
+        self.graph = graph
+        self.out_dev = out_dev
+        self.workspace = workspace
+
+
+def q_local_is_whole(lo: int, hi: int, num_kv_heads: int) -> bool:
+    return (lo, hi) == (0, num_kv_heads)
 
 
 def _default_device() -> torch.device:
@@ -104,7 +121,7 @@ class B200AttentionBackend:
                  device=None, kv_cache_fraction: float = 0.5, partition_tokens: int = 0,
                  shard=None, check_status: bool = True, shuffle_seed: Optional[int] = None,
                  gather: str = "peer", max_rows_per_call: Optional[int] = None,
-                 **_unused) -> None:
+                 cuda_graphs: bool = True, **_unused) -> None:
         self.device = torch.device(device) if device is not None else _default_device()
         if self.device.type != "cuda":
             raise RuntimeError("B200AttentionBackend requires a CUDA device (no CPU fallback)")
@@ -135,6 +152,7 @@ class B200AttentionBackend:
         self._status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         self._kv_esz = 0
         self._fast: Dict[tuple, _FastPlan] = {}
+        self.cuda_graphs = bool(cuda_graphs)
 
     # ------------------------------------------------------------ setup
     def _ensure_pool(self, num_layers: int, heads: int, head_dim: int, dtype: torch.dtype) -> None:
@@ -294,19 +312,93 @@ class B200AttentionBackend:
             srcs[2 * B + i] = vt.data_ptr()
         plan.meta[:] = rows + offs + ctx_rows
         _lib.host_gather(srcs, plan.sizes, plan.n, plan.host.data_ptr())
-        plan.dev.copy_(plan.host, non_blocking=True)
-        out = self._launch(reqs, layer, n_new, targets, plan.q, plan.k, plan.v, plan.rows,
-                           plan.offs, plan.ctx, scale, check=False)
-        # output and status word back behind one synchronisation
-        oh = plan.out
-        oh.copy_(out, non_blocking=True)
-        self._status_host.copy_(self.pool.status, non_blocking=True)
+        step = self._step_graph(plan, layer, scale, max(targets)) if plan.warm else None
+        if step is not None:
+            # one graph launch: H2D, fused step, D2H of output and status
+            step.graph.replay()
+            self._advance(reqs, layer, n_new, targets)
+        else:
+            plan.dev.copy_(plan.host, non_blocking=True)
+            out = self._launch(reqs, layer, n_new, targets, plan.q, plan.k, plan.v, plan.rows,
+                               plan.offs, plan.ctx, scale, check=False)
+            # output and status word back behind one synchronisation
+            plan.out.copy_(out, non_blocking=True)
+            self._status_host.copy_(self.pool.status, non_blocking=True)
+            plan.warm = True
         torch.cuda.current_stream(self.device).synchronize()
         if self.check_status and int(self._status_host[0]):
             self.pool.check_status()
-        res = oh.clone()
-        for n in range(B):
-            results[base + n] = res[n:n + 1]
+        results[base:base + B] = plan.out.clone().split(1)
+
+    # Context lengths are rounded up to this many tokens for a captured step:
+    # the launch's max_ctx_len (and so its partition plan and workspace) is
+    # fixed per graph, re-captured when the batch outgrows it.
+    _GRAPH_CTX_BUCKET = 512
+
+    def _step_graph(self, plan: _FastPlan, layer: int, scale: float, max_ctx: int):
+        """The captured step for this batch shape, layer, scale and context
+        bucket, capturing it on first use; None where a step is not captured
+        (graphs off, NCCL-gathered shards)."""
+        if not self.cuda_graphs:
+            return None
+        bucket = -(-max_ctx // self._GRAPH_CTX_BUCKET) * self._GRAPH_CTX_BUCKET
+        key = (layer, scale, bucket)
+        step = plan.graphs.get(key)
+        if step is not None:
+            return step
+        pool = self.pool
+        sharded = self.shard is not None and self.shard.world > 1
+        group = plan.q.shape[1] // self.num_kv_heads
+        lo, hi = self.kv_range
+        q = plan.q if q_local_is_whole(lo, hi, self.num_kv_heads) else plan.q[:, lo * group:hi * group]
+        if q.dtype not in (torch.float32, self.kv_dtype) or q.stride(2) != 1 or q.stride(1) != self.head_dim:
+            return None
+        peer = self._peer_for(q) if sharded else None
+        if sharded and peer is None:
+            return None  # NCCL gather: stays eager
+        B = q.shape[0]
+        if plan.k.shape[1] != self.num_kv_heads or plan.k.dtype != self.kv_dtype:
+            return None  # K/V need a copy (expanded heads, other dtype): stays eager
+        k_loc, v_loc = plan.k[:, lo:hi], plan.v[:, lo:hi]  # token stride spans all heads
+        n_seqs = B
+        if peer is not None:
+            nbytes = _lib.decode_gather_workspace_bytes(n_seqs, B, 1, bucket, q.shape[1], pool.num_kv_heads,
+                                                        self.head_dim, pool.block_size, pool.dtype,
+                                                        q.dtype, self.partition_tokens)
+        else:
+            nbytes = _lib.decode_workspace_bytes(n_seqs, B, 1, bucket, q.shape[1], pool.num_kv_heads,
+                                                 self.head_dim, pool.block_size, pool.dtype, q.dtype,
+                                                 self.partition_tokens)
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=self.device) if nbytes > 0 else None
+        out_dev = None if peer is not None else torch.empty_like(q)
+        for old in [k for k in plan.graphs if k[:2] == key[:2]]:
+            del plan.graphs[old]  # an older bucket of this layer and scale
+        g = torch.cuda.CUDAGraph()
+        try:
+            with torch.cuda.graph(g):
+                plan.dev.copy_(plan.host, non_blocking=True)
+                if peer is not None:
+                    _lib.decode_step_gather(q, pool.k[layer], pool.v[layer], k_loc, v_loc, pool.tables,
+                                            plan.offs, plan.ctx, peer, max_queries_per_seq=1,
+                                            max_ctx_len=bucket, score_scale=scale, seq_rows=plan.rows,
+                                            partition_tokens=self.partition_tokens, workspace=ws,
+                                            status=pool.status)
+                    src = peer.out[:B]
+                else:
+                    _lib.decode_step(out_dev, q, pool.k[layer], pool.v[layer], k_loc, v_loc, pool.tables,
+                                     plan.offs, plan.ctx, max_queries_per_seq=1, max_ctx_len=bucket,
+                                     score_scale=scale, seq_rows=plan.rows,
+                                     partition_tokens=self.partition_tokens, workspace=ws,
+                                     status=pool.status, check=False)
+                    src = out_dev
+                plan.out.copy_(src, non_blocking=True)
+                self._status_host.copy_(pool.status, non_blocking=True)
+        except Exception:
+            self.cuda_graphs = False  # capture is not available here: stay eager from now on
+            return None
+        step = _StepGraph(g, out_dev, ws)
+        plan.graphs[key] = step
+        return step
 
     # ------------------------------------------------------------ tensor API
     def decode_batch(self, request_ids: Sequence[str], layer_idx: int, query: torch.Tensor,
@@ -383,6 +475,15 @@ class B200AttentionBackend:
             out = pool.decode_step(layer_idx, q, self._local_kv(key), self._local_kv(value), offs_d,
                                    ctx_d, rows_d, max(n_new), max(targets), score_scale,
                                    partition_tokens=self.partition_tokens, check=check)
+        self._advance(reqs, layer_idx, n_new, targets)
+        if sharded and peer is None:
+            out = self.shard.gather(out, self.num_kv_heads, group)
+        return out
+
+    def _advance(self, reqs, layer_idx, n_new, targets) -> None:
+        """Host bookkeeping of a launched step: per-layer lengths, context
+        (after the last layer) and counters."""
+        lo, hi = self.kv_range
         for r, n in zip(reqs, n_new):
             r.layer_len[layer_idx] += n
             if layer_idx == self.num_layers - 1:
@@ -392,9 +493,6 @@ class B200AttentionBackend:
         st.items += len(reqs)
         st.tokens += sum(n_new)
         st.kv_bytes_read += sum(targets) * (hi - lo) * self.head_dim * 2 * self._kv_esz
-        if sharded and peer is None:
-            out = self.shard.gather(out, self.num_kv_heads, group)
-        return out
 
     def _peer_for(self, q: torch.Tensor):
         """The fused-gather buffers for this call's shape, or None (NCCL)."""

@@ -112,7 +112,9 @@ def _worker(rank, world, port, q_out):
         for be in bes:
             for rid, layers in kv.items():
                 be.init_request(rid, layers)
-        for layer in range(2):
+        # two steps of two layers: the first call of the batch shape runs eagerly,
+        # later ones capture and replay the fused step as a CUDA graph
+        for layer in [0, 1, 0, 1]:
             items = [{"request_id": rid, "layer_idx": layer, "score_scale": 1 / math.sqrt(D),
                       "query": torch.randn(hq, D, generator=gen),
                       "key": torch.randn(hkv, D, generator=gen).bfloat16(),
@@ -121,6 +123,7 @@ def _worker(rank, world, port, q_out):
             o1 = bes[1].decode_layer_batch(items)
             errs.append(max(float((x - y).abs().max()) for x, y in zip(o0, o1)))
         assert bes[1]._peer is not None
+        assert all(p.graphs for p in bes[1]._fast.values())  # the sharded step was captured
         bes[1].close()
         q_out.put((rank, int(st.item()), errs))
     except Exception as e:
