@@ -90,12 +90,17 @@ class _FastPlan:
         self.out = torch.empty((B, hq_total, q_shape[-1]), dtype=out_dtype, pin_memory=True)
         self.warm = False  # one eager call ran with this shape (one-time set-up done)
         self.graphs: Dict[tuple, "_StepGraph"] = {}
+        # device output and split-K workspace (per context bucket) shared by
+        # this shape's graphs: they replay one after another on one stream
+        self.out_dev: Optional[torch.Tensor] = None
+        self.ws: Dict[int, Optional[torch.Tensor]] = {}
 
 
 class _StepGraph:
     """A captured fast-path step: H2D of the staging buffer, the fused
     append + decode (+ reduce, + gather), D2H of the output and the status
-    word.  Owns the output and workspace its kernels were captured with."""
+    word.  Holds the output and workspace its kernels were captured with, so
+    they stay allocated while the graph exists."""
 
     def __init__(self, graph, out_dev, workspace):
         self.graph = graph
@@ -369,10 +374,18 @@ class B200AttentionBackend:
             nbytes = _lib.decode_workspace_bytes(n_seqs, B, 1, bucket, q.shape[1], pool.num_kv_heads,
                                                  self.head_dim, pool.block_size, pool.dtype, q.dtype,
                                                  self.partition_tokens)
-        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=self.device) if nbytes > 0 else None
-        out_dev = None if peer is not None else torch.empty_like(q)
         for old in [k for k in plan.graphs if k[:2] == key[:2]]:
             del plan.graphs[old]  # an older bucket of this layer and scale
+        live = {k[2] for k in plan.graphs}
+        for b in [b for b in plan.ws if b not in live]:
+            del plan.ws[b]  # graphs that still use it keep their own reference
+        if bucket not in plan.ws:
+            plan.ws[bucket] = (torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+                               if nbytes > 0 else None)
+        ws = plan.ws[bucket]
+        if peer is None and plan.out_dev is None:
+            plan.out_dev = torch.empty_like(q)
+        out_dev = None if peer is not None else plan.out_dev
         g = torch.cuda.CUDAGraph()
         try:
             with torch.cuda.graph(g):
