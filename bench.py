@@ -43,10 +43,10 @@ METRIC = "paged decode-attn KV-read GB/s"
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one
 # paged_decode_mma_kernel launch from an ncu capture of the same workload and
-# kernel build: (config, GPUs) -> (bytes, summary file).
+# kernel build: (config, GPUs, KV dtype option) -> (bytes, summary file).
 NCU_TRAFFIC = {
-    ("c3", 1): (1.0740e9 + 8.032e6, "profiles/paged_decode_mma_c3_full.md"),
-    ("c3", 8): (134.363e6 + 3.985e6, "profiles/paged_decode_mma_c3_shard8_full.md"),
+    ("c3", 1, "config"): (1.0740e9 + 8.032e6, "profiles/paged_decode_mma_c3_full.md"),
+    ("c3", 8, "config"): (134.363e6 + 3.985e6, "profiles/paged_decode_mma_c3_shard8_full.md"),
 }
 
 
@@ -110,6 +110,16 @@ class ClockSampler:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def config_for(args):
+    """The workload of ``--config``, with the KV cache in fp8 under ``--kv-dtype fp8``."""
+    import dataclasses
+    from cloverinfer_b200.workloads import CONFIGS
+    cfg = CONFIGS[args.config]
+    if getattr(args, "kv_dtype", "config") == "fp8":
+        cfg = dataclasses.replace(cfg, name=cfg.name + "-fp8kv", dtype=torch.float8_e4m3fn)
+    return cfg
 
 
 def _dist_setup():
@@ -177,7 +187,7 @@ def run_reference(args):
     if rank != 0:
         return
     from cloverinfer_b200.workloads import CONFIGS, context_lengths, kv_bytes
-    cfg = CONFIGS[args.config]
+    cfg = config_for(args)
     lens = context_lengths(cfg, 0)
     nbytes = kv_bytes(lens, cfg.num_kv_heads, cfg.head_dim, cfg.dtype)
     per_step = []
@@ -222,7 +232,7 @@ def run_b200(args):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     _lib.lib()
-    cfg = CONFIGS[args.config]
+    cfg = config_for(args)
     lens = context_lengths(cfg, 0, args.batch)
     n_new = new_tokens(cfg, 0, args.batch)
     B = len(lens)
@@ -353,8 +363,9 @@ def run_b200(args):
         "pct_hbm_peak_per_gpu": round(100.0 * value / world / hbm_peak, 2),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4),
-                     "traffic": NCU_TRAFFIC.get((args.config, world), (None,))[0],
-                     "traffic_source": NCU_TRAFFIC.get((args.config, world), (None, None))[1],
+                     "traffic": NCU_TRAFFIC.get((args.config, world, args.kv_dtype), (None,))[0],
+                     "traffic_source": NCU_TRAFFIC.get((args.config, world, args.kv_dtype),
+                                                       (None, None))[1],
                      "kernel": "paged_decode_mma_kernel + splitk_reduce_kernel",
                      "launch_ms": round(dec_ms, 5), "peak_kind": peak_kind},
         "clocks": clk,
@@ -462,6 +473,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kv-dtype", default="config", choices=["config", "fp8"],
+                    help="KV cache dtype: the configuration's, or fp8 (e4m3) on the same workload")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="N>1 output all-gather: fused NVLink peer stores or NCCL")
     args = ap.parse_args()

@@ -32,8 +32,9 @@ DEV_CTX_RANGE = 0x20
 
 PARTITION_BALANCED = -1  # CLOVER_B200_PARTITION_BALANCED: the balanced split
 
-F32, F16, BF16 = 0, 1, 2
-_DTYPE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+F32, F16, BF16, FP8_E4M3 = 0, 1, 2, 3
+_DTYPE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16,
+          torch.float8_e4m3fn: FP8_E4M3}  # fp8: KV caches only
 
 # Every symbol include/clover_b200.h declares: name -> (restype, argtypes)
 _P = ctypes.c_void_p

@@ -171,7 +171,7 @@ class B200AttentionBackend:
         if heads % hkv:
             raise ValueError(f"initial_kv has {heads} heads, not a multiple of num_kv_heads={hkv}")
         dt = self.kv_dtype or dtype
-        if dt not in (torch.float32, torch.float16, torch.bfloat16):
+        if dt not in (torch.float32, torch.float16, torch.bfloat16, torch.float8_e4m3fn):
             raise TypeError(f"unsupported KV dtype {dt}")
         self.num_layers, self.num_kv_heads, self.head_dim, self.kv_dtype = num_layers, hkv, head_dim, dt
         self._kv_esz = torch.empty((), dtype=dt).element_size()

@@ -8,6 +8,8 @@
 #include <mutex>
 #include <utility>
 
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 
 namespace clover {
@@ -140,20 +142,28 @@ __device__ __forceinline__ void store_out(const DecodeArgs& a, int64_t idx, floa
 
 // ------------------------------------------------------------------ tensor-core path
 // One pipeline stage holds BPS consecutive KV blocks (K and V tiles) of one KV
-// head: kTok = BPS * BS token rows of D bf16/fp16 values, stored per 64-column
-// chunk as 128-byte rows with the TMA 128-byte swizzle.
-template <int D, int BS, int NT = 1>
+// head: kTok = BPS * BS token rows of D values, stored per 128-byte chunk of
+// a row (64 bf16/fp16 values, or 128 fp8 values) with the TMA 128-byte
+// swizzle.  An fp8 cache (F8) adds one fp16 staging stage (K and V) per warp
+// that each landed stage is converted into before the tensor-core step.
+template <int D, int BS, int NT = 1, bool F8 = false>
 struct MmaGeom {
-  static constexpr int kChunks = D / 64;  // 128-byte swizzle atoms per row
+  static constexpr int kEsz = F8 ? 1 : 2;            // bytes per cached value
+  static constexpr int kChunkVals = 128 / kEsz;       // values per 128-byte chunk
+  static constexpr int kChunks = D / kChunkVals;      // TMA boxes per tile
   static constexpr int kBps = (CLOVER_MMA_STAGE_TOKENS > BS ? CLOVER_MMA_STAGE_TOKENS : BS) / BS;
   static constexpr int kTok = kBps * BS;   // tokens per stage
-  static constexpr int kTile = kTok * D * 2;
+  static constexpr int kTile = kTok * D * kEsz;
   static constexpr int kStage = 2 * kTile;  // K + V
-  // keep the ring within the per-CTA shared memory limit
-  static constexpr int kStages = kMmaWarps * CLOVER_MMA_STAGES * kStage <= 200 * 1024
-                                     ? CLOVER_MMA_STAGES
-                                     : (kMmaWarps * 2 * kStage <= 200 * 1024 ? 2 : 1);
-  static constexpr int kPipeBytes = kMmaWarps * kStages * kStage;
+  static constexpr int kConv = F8 ? 2 * kTok * D * 2 : 0;  // fp16 staging (K + V)
+  // keep the ring within the per-CTA shared memory limit; fp8 rings are
+  // deeper (their stages are half the bytes)
+  static constexpr int kWant = F8 ? 3 * CLOVER_MMA_STAGES / 2 : CLOVER_MMA_STAGES;
+  static constexpr int kStages = kMmaWarps * (kWant * kStage + kConv) <= 200 * 1024
+                                     ? kWant
+                                     : (kMmaWarps * (2 * kStage + kConv) <= 200 * 1024 ? 2 : 1);
+  static constexpr int kWarpBytes = kStages * kStage + kConv;
+  static constexpr int kPipeBytes = kMmaWarps * kWarpBytes;
   static constexpr int kCols = kMmaCols * NT;  // columns per warp (NT n-tiles)
   static constexpr int kRedBytes = kMmaWarps * kCols * (D + 4) * 4 + 2 * kMmaWarps * kCols * 4;
   static constexpr int kSmem = (kPipeBytes > kRedBytes ? kPipeBytes : kRedBytes) + 1024;
@@ -165,6 +175,33 @@ template <int TOK>
 __device__ __forceinline__ uint32_t swz(int r, int cg) {
   const int c64 = cg >> 3, c = cg & 7;
   return (uint32_t)(c64 * TOK * 128 + r * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// Expand one landed fp8 (e4m3) tile — TOK rows of D bytes, 128-byte
+// swizzled per 128-value chunk — into the fp16 layout the tensor-core step
+// reads (swz).  e4m3 values are exact in fp16.  One warp; 16 values per
+// lane and step.
+template <int D, int TOK>
+__device__ __forceinline__ void expand_fp8_tile(const uint8_t* src, uint8_t* dst, int lane) {
+  constexpr int kUnits = D / 16;  // 16-byte fp8 units per row
+#pragma unroll 4
+  for (int i = lane; i < TOK * kUnits; i += 32) {
+    const int r = i / kUnits, u = i - r * kUnits;
+    const int c8 = u >> 3, uu = u & 7;
+    const uint4 raw = *reinterpret_cast<const uint4*>(src + c8 * TOK * 128 + r * 128 + ((uu ^ (r & 7)) << 4));
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    uint32_t h[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[j] & 0xffffu), __NV_E4M3);
+      const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[j] >> 16), __NV_E4M3);
+      h[2 * j] = (uint32_t)lo.x | ((uint32_t)lo.y << 16);
+      h[2 * j + 1] = (uint32_t)hi.x | ((uint32_t)hi.y << 16);
+    }
+    const int cg = u * 2;  // 8-value fp16 units of this row
+    *reinterpret_cast<uint4*>(dst + swz<TOK>(r, cg)) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(dst + swz<TOK>(r, cg + 1)) = make_uint4(h[4], h[5], h[6], h[7]);
+  }
 }
 
 // Per-warp column state of the tensor-core path: NT n-tiles of 8 columns.
@@ -424,10 +461,11 @@ int stream_decode(int kv_dtype, int q_dtype, int D, int BS, int cols, const Deco
 
 // CTAs per SM the tensor-core kernels are compiled for: 16-column warps keep
 // twice the accumulators (and run 3 CTAs per SM at block 32, whose stages
-// are twice as large).
-template <int D, int NT>
+// are twice as large); an fp8 cache's warps hold a deeper ring plus an fp16
+// staging stage (5 CTAs per SM).
+template <int D, int NT, bool F8 = false>
 constexpr int mma_min_ctas() {
-  return D >= 256 ? 1 : (NT > 1 ? 3 : CLOVER_MMA_MIN_CTAS);
+  return D >= 256 ? 1 : (NT > 1 ? 3 : (F8 ? 5 : CLOVER_MMA_MIN_CTAS));
 }
 
 }  // namespace clover

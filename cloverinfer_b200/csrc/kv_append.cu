@@ -79,6 +79,7 @@ extern "C" int clover_b200_kv_append(void* k_cache, void* v_cache, const void* k
     case CLOVER_B200_F32: esz = 4; break;
     case CLOVER_B200_F16:
     case CLOVER_B200_BF16: esz = 2; break;
+    case CLOVER_B200_FP8_E4M3: esz = 1; break;
     default: return set_error(CLOVER_B200_ERR_UNSUPPORTED, "kv_append: dtype %d", dtype);
   }
   const int32_t row_elems = num_kv_heads * head_dim;
@@ -108,9 +109,13 @@ extern "C" int clover_b200_kv_append(void* k_cache, void* v_cache, const void* k
       kv_append_elem_kernel<uint32_t><<<blocks, threads, 0, s>>>(
           (uint32_t*)k_cache, (uint32_t*)v_cache, (const uint32_t*)k_new, (const uint32_t*)v_new,
           new_token_stride, slot_mapping, n_tokens, row_elems, n_slots, dev_status);
-    } else {
+    } else if (esz == 2) {
       kv_append_elem_kernel<uint16_t><<<blocks, threads, 0, s>>>(
           (uint16_t*)k_cache, (uint16_t*)v_cache, (const uint16_t*)k_new, (const uint16_t*)v_new,
+          new_token_stride, slot_mapping, n_tokens, row_elems, n_slots, dev_status);
+    } else {
+      kv_append_elem_kernel<uint8_t><<<blocks, threads, 0, s>>>(
+          (uint8_t*)k_cache, (uint8_t*)v_cache, (const uint8_t*)k_new, (const uint8_t*)v_new,
           new_token_stride, slot_mapping, n_tokens, row_elems, n_slots, dev_status);
     }
   }

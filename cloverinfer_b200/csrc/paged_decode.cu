@@ -196,11 +196,11 @@ __device__ __forceinline__ void merge_store_rt(const DecodeArgs& a, const CtaWor
 }
 
 
-template <typename T, bool QF32, int D, int BS, int NT>
-__global__ void __launch_bounds__(kMmaThreads, mma_min_ctas<D, NT>())
+template <typename T, bool QF32, int D, int BS, int NT, bool F8>
+__global__ void __launch_bounds__(kMmaThreads, mma_min_ctas<D, NT, F8>())
 paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const DecodeArgs a) {
-  using G = MmaGeom<D, BS, NT>;
+  using G = MmaGeom<D, BS, NT, F8>;
   constexpr int NW = kMmaWarps;
   constexpr int STAGES = G::kStages;
   constexpr int BPS = G::kBps;
@@ -291,8 +291,10 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   }
   __syncthreads();
 
-  const uint32_t ring = smem_addr(smem) + warp * STAGES * G::kStage;
+  const uint32_t ring = smem_addr(smem) + warp * G::kWarpBytes;
   const uint32_t bar0 = smem_addr(&bars[warp * STAGES]);
+  // fp8 cache: the fp16 staging stage (K then V) after this warp's ring
+  const uint32_t conv = ring + STAGES * G::kStage;
 
   // Fetch this warp's k-th stage group (all lanes call: the ids are shuffled).
   auto issue = [&](int k) {
@@ -307,15 +309,15 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
       int nb = 0;
 #pragma unroll
       for (int i = 0; i < BPS; ++i) nb += ids[i] >= 0;
-      mbar_arrive_expect_tx(bar, nb * 2 * BS * D * 2);
+      mbar_arrive_expect_tx(bar, nb * 2 * BS * D * G::kEsz);
 #pragma unroll
       for (int i = 0; i < BPS; ++i) {
         if (ids[i] < 0) continue;
 #pragma unroll
         for (int c = 0; c < G::kChunks; ++c) {
           const uint32_t off = c * TOK * 128 + i * BS * 128;
-          tma_load_3d(kd + off, &tmK, c * 64, w.kvh, ids[i] * BS, bar);
-          tma_load_3d(vd + off, &tmV, c * 64, w.kvh, ids[i] * BS, bar);
+          tma_load_3d(kd + off, &tmK, c * G::kChunkVals, w.kvh, ids[i] * BS, bar);
+          tma_load_3d(vd + off, &tmV, c * G::kChunkVals, w.kvh, ids[i] * BS, bar);
         }
       }
     }
@@ -340,13 +342,27 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
       break;
     }
     consumed = k + 1;
-    const uint32_t ks = ring + s * G::kStage;
-    const uint32_t vs = ks + G::kTile;
+    uint32_t ks = ring + s * G::kStage;
+    uint32_t vs = ks + G::kTile;
+    if (F8) {
+      // expand the landed fp8 stage into the fp16 staging stage, then the
+      // ring slot is free for the next copy
+      uint8_t* base = smem - smem_addr(smem);
+      expand_fp8_tile<D, TOK>(base + ks, base + conv, lane);
+      expand_fp8_tile<D, TOK>(base + vs, base + conv + TOK * D * 2, lane);
+      __syncwarp();
+      if (k + STAGES < n_mine) {
+        issue(k + STAGES);
+        ++issued;
+      }
+      ks = conv;
+      vs = conv + TOK * D * 2;
+    }
     const int tok0 = w.tok_begin + (warp + k * NW) * TOK;
     mma_stage<T, QF32, D, TOK, NT>(ks, vs, smem + (vs - smem_addr(smem)), tok0,
                                    w.tok_end - tok0, a.scale_log2, c, lane);
     __syncwarp();
-    if (k + STAGES < n_mine) {
+    if (!F8 && k + STAGES < n_mine) {
       issue(k + STAGES);
       ++issued;
     }
@@ -722,11 +738,15 @@ static int get_tmap(const void* ptr, int dtype, int D, int H, int BS, int64_t nb
   }
   CUtensorMap m;
   const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)(nb * BS)};
-  const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)H * D * 2};
-  const cuuint32_t box[3] = {64, 1, (cuuint32_t)BS};
+  // 128-byte rows of the swizzle: 64 two-byte values or 128 fp8 values
+  const cuuint64_t esz = dtype == CLOVER_B200_FP8_E4M3 ? 1 : 2;
+  const cuuint64_t strides[2] = {(cuuint64_t)D * esz, (cuuint64_t)H * D * esz};
+  const cuuint32_t box[3] = {(cuuint32_t)(128 / esz), 1, (cuuint32_t)BS};
   const cuuint32_t estr[3] = {1, 1, 1};
   const CUtensorMapDataType dt =
-      dtype == CLOVER_B200_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+      dtype == CLOVER_B200_BF16      ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+      : dtype == CLOVER_B200_FP8_E4M3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUresult r = g_encode(&m, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -740,6 +760,9 @@ static int get_tmap(const void* ptr, int dtype, int D, int H, int BS, int64_t nb
 }
 
 static bool mma_supported(int kv_dtype, int q_dtype, int D, int BS) {
+  if (kv_dtype == CLOVER_B200_FP8_E4M3)  // read as fp16: fp32 or fp16 queries
+    return (q_dtype == CLOVER_B200_F32 || q_dtype == CLOVER_B200_F16) && (D == 128 || D == 256) &&
+           (BS == 16 || BS == 32);
   return (kv_dtype == CLOVER_B200_BF16 || kv_dtype == CLOVER_B200_F16) &&
          (q_dtype == CLOVER_B200_F32 || q_dtype == kv_dtype) && (D == 64 || D == 128 || D == 256) &&
          (BS == 16 || BS == 32);
@@ -787,12 +810,12 @@ static int choose_partition(int max_ctx, int BS, int rows_x_kvh, bool mma) {
 }
 
 
-template <typename T, bool QF32, int D, int BS, int NT>
+template <typename T, bool QF32, int D, int BS, int NT, bool F8 = false>
 static int launch_mma(const DecodeArgs& a, const CUtensorMap& tk, const CUtensorMap& tv,
                       dim3 grid, cudaStream_t s) {
-  using G = MmaGeom<D, BS, NT>;
+  using G = MmaGeom<D, BS, NT, F8>;
   static uint64_t configured = 0;  // one bit per device ordinal
-  auto kern = paged_decode_mma_kernel<T, QF32, D, BS, NT>;
+  auto kern = paged_decode_mma_kernel<T, QF32, D, BS, NT, F8>;
   int dev = 0;
   int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   if (rc) return rc;
@@ -826,6 +849,23 @@ static int dispatch_d(int D, int BS, const DecodeArgs& a, const CUtensorMap& tk,
                   : dispatch_bs<T, QF32, 128, 1>(BS, a, tk, tv, grid, s);
     default: return dispatch_bs<T, QF32, 256, 1>(BS, a, tk, tv, grid, s);
   }
+}
+
+// fp8 cache: fp16 tensor-core step on the expanded stages (head_dim 128, 8 or
+// 16 columns, or 256).
+template <bool QF32, int D, int NT>
+static int dispatch_bs_f8(int BS, const DecodeArgs& a, const CUtensorMap& tk,
+                          const CUtensorMap& tv, dim3 grid, cudaStream_t s) {
+  return BS == 16 ? launch_mma<__half, QF32, D, 16, NT, true>(a, tk, tv, grid, s)
+                  : launch_mma<__half, QF32, D, 32, NT, true>(a, tk, tv, grid, s);
+}
+
+template <bool QF32>
+static int dispatch_d_f8(int D, int BS, const DecodeArgs& a, const CUtensorMap& tk,
+                         const CUtensorMap& tv, dim3 grid, cudaStream_t s) {
+  if (D == 256) return dispatch_bs_f8<QF32, 256, 1>(BS, a, tk, tv, grid, s);
+  return a.cols_per_cta > kMmaCols ? dispatch_bs_f8<QF32, 128, 2>(BS, a, tk, tv, grid, s)
+                                   : dispatch_bs_f8<QF32, 128, 1>(BS, a, tk, tv, grid, s);
 }
 
 template <typename KT, int EPL>
@@ -879,11 +919,16 @@ static int make_plan(int n_seqs, int n_rows, int max_q, int max_ctx, int hq, int
     return set_error(CLOVER_B200_ERR_INVALID_ARG, "paged_decode: num_q_heads %% num_kv_heads != 0");
   if (q_dtype != CLOVER_B200_F32 && q_dtype != CLOVER_B200_F16 && q_dtype != CLOVER_B200_BF16)
     return set_error(CLOVER_B200_ERR_UNSUPPORTED, "paged_decode: q dtype %d", q_dtype);
-  if (kv_dtype != CLOVER_B200_F32 && kv_dtype != CLOVER_B200_F16 && kv_dtype != CLOVER_B200_BF16)
+  if (kv_dtype != CLOVER_B200_F32 && kv_dtype != CLOVER_B200_F16 && kv_dtype != CLOVER_B200_BF16 &&
+      kv_dtype != CLOVER_B200_FP8_E4M3)
     return set_error(CLOVER_B200_ERR_UNSUPPORTED, "paged_decode: kv dtype %d", kv_dtype);
   if (max_q == 0) max_q = 1;
   const int group = hq / hkv;
   pl->mma = mma_supported(kv_dtype, q_dtype, D, BS);
+  if (kv_dtype == CLOVER_B200_FP8_E4M3 && !pl->mma)
+    return set_error(CLOVER_B200_ERR_UNSUPPORTED,
+                     "paged_decode: an fp8 cache needs head_dim 128/256, block 16/32 and fp32 or "
+                     "fp16 queries (got D=%d, block %d, q dtype %d)", D, BS, q_dtype);
   if (!pl->mma && D > 256)
     return set_error(CLOVER_B200_ERR_UNSUPPORTED, "paged_decode: head_dim %d > 256", D);
   const int ncols_seq = max_q * group;
@@ -909,7 +954,8 @@ static int make_plan(int n_seqs, int n_rows, int max_q, int max_ctx, int hq, int
   pl->part_tokens = pt;
   pl->max_parts = max_ctx > 0 ? (max_ctx + pt - 1) / pt : 1;
   pl->stream = false;
-  if (want_stream && pl->mma && MmaGeomBps(BS) == 1 && n_seqs <= kStreamMaxSeqs) {
+  if (want_stream && pl->mma && kv_dtype != CLOVER_B200_FP8_E4M3 && MmaGeomBps(BS) == 1 &&
+      n_seqs <= kStreamMaxSeqs) {
     // Stream decomposition: units of one block; a segment of n units spread
     // over `per`-unit worker ranges has at most min(n, workers / segments
     // per sequence + 1) parts.  Unit keys pack (segment << 16 | block).
@@ -1044,7 +1090,7 @@ static int decode_impl(
   a.k_new = nullptr;
   a.v_new = nullptr;
   a.new_stride = new_token_stride;
-  a.kv_esz = kv_dtype == CLOVER_B200_F32 ? 4 : 2;
+  a.kv_esz = kv_dtype == CLOVER_B200_F32 ? 4 : (kv_dtype == CLOVER_B200_FP8_E4M3 ? 1 : 2);
   a.force_split = gather != nullptr;
   a.n_seqs = n_seqs;
   a.max_ctx = max_ctx_len;
@@ -1100,7 +1146,11 @@ static int decode_impl(
     if (rc) return rc;
     rc = get_tmap(v_cache, kv_dtype, head_dim, num_kv_heads, block_size, num_blocks, &tv);
     if (rc) return rc;
-    if (kv_dtype == CLOVER_B200_BF16) {
+    if (kv_dtype == CLOVER_B200_FP8_E4M3) {
+      rc = q_dtype == CLOVER_B200_F32
+               ? dispatch_d_f8<true>(head_dim, block_size, a, tk, tv, grid, s)
+               : dispatch_d_f8<false>(head_dim, block_size, a, tk, tv, grid, s);
+    } else if (kv_dtype == CLOVER_B200_BF16) {
       rc = q_dtype == CLOVER_B200_F32
                ? dispatch_d<__nv_bfloat16, true>(head_dim, block_size, a, tk, tv, grid, s)
                : dispatch_d<__nv_bfloat16, false>(head_dim, block_size, a, tk, tv, grid, s);

@@ -61,6 +61,11 @@ extern "C" {
 #define CLOVER_B200_F32  0
 #define CLOVER_B200_F16  1
 #define CLOVER_B200_BF16 2
+/* KV cache only: 1-byte e4m3 values (no scale; values are stored as given),
+ * read by the decode as exact fp16.  Queries and outputs stay F32 or F16;
+ * the decode takes it on the tensor-core path (head_dim 128 or 256, block
+ * 16 or 32).  No counterpart in the reference, which keeps fp16/fp32 caches. */
+#define CLOVER_B200_FP8_E4M3 3
 
 /* Library version (major*10000 + minor*100 + patch). */
 CLOVER_B200_API int clover_b200_version(void);
