@@ -36,6 +36,8 @@ from __future__ import annotations
 
 import math
 import os
+import warnings
+from collections import OrderedDict
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Sequence
 
@@ -126,7 +128,7 @@ class B200AttentionBackend:
                  device=None, kv_cache_fraction: float = 0.5, partition_tokens: int = 0,
                  shard=None, check_status: bool = True, shuffle_seed: Optional[int] = None,
                  gather: str = "peer", max_rows_per_call: Optional[int] = None,
-                 cuda_graphs: bool = True, **_unused) -> None:
+                 cuda_graphs: bool = True, max_fast_plans: int = 8, **_unused) -> None:
         self.device = torch.device(device) if device is not None else _default_device()
         if self.device.type != "cuda":
             raise RuntimeError("B200AttentionBackend requires a CUDA device (no CPU fallback)")
@@ -156,7 +158,11 @@ class B200AttentionBackend:
         self.stats = _Stats()
         self._status_host = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         self._kv_esz = 0
-        self._fast: Dict[tuple, _FastPlan] = {}
+        # host-tensor fast-path plans (staging buffers, captured steps) by batch
+        # shape, least recently used first; continuous batching changes the
+        # batch size from step to step, so only the most recent shapes are kept
+        self._fast: "OrderedDict[tuple, _FastPlan]" = OrderedDict()
+        self.max_fast_plans = int(max_fast_plans)
         self.cuda_graphs = bool(cuda_graphs)
 
     # ------------------------------------------------------------ setup
@@ -305,6 +311,11 @@ class B200AttentionBackend:
             plan = _FastPlan(self.device, B, q0.shape, q_dtype, k0.shape, k0.dtype, 3 * B + 1,
                              q_dtype, q0.shape[0])
             self._fast[key] = plan
+            while len(self._fast) > max(1, self.max_fast_plans):
+                # every call ends with a stream sync, so no evicted graph is in flight
+                self._fast.popitem(last=False)
+        else:
+            self._fast.move_to_end(key)
         # one native gather into the pinned staging buffer -> one H2D copy
         srcs = plan.srcs
         for i in range(B):
@@ -406,8 +417,10 @@ class B200AttentionBackend:
                     src = out_dev
                 plan.out.copy_(src, non_blocking=True)
                 self._status_host.copy_(pool.status, non_blocking=True)
-        except Exception:
-            self.cuda_graphs = False  # capture is not available here: stay eager from now on
+        except Exception as e:  # capture is not available here: stay eager from now on
+            warnings.warn(f"B200AttentionBackend: CUDA graph capture failed ({e!r}); "
+                          "using eager launches", RuntimeWarning)
+            self.cuda_graphs = False
             return None
         step = _StepGraph(g, out_dev, ws)
         plan.graphs[key] = step

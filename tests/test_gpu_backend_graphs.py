@@ -61,3 +61,34 @@ def test_graph_path_matches_eager_and_oracle():
         ref = attend(it["query"][0].float(), repeat_kv(lay["key"], 4), repeat_kv(lay["value"], 4), 0.088)
         assert_attn_close(res[i][0], ref, what=f"seq {i}")
     assert be.get_context_len("s0") == 500 + 24
+
+
+def test_plan_cache_is_bounded_and_stays_correct():
+    """Continuous batching changes the batch size every step: only the most
+    recent ``max_fast_plans`` shapes keep staging buffers and graphs."""
+    from cloverinfer_b200 import B200AttentionBackend
+    hq, hkv, D = 8, 2, 128
+    be = B200AttentionBackend(num_blocks=128, block_size=16, num_kv_heads=hkv,
+                              kv_dtype=torch.bfloat16, device="cuda", max_seqs=4,
+                              max_fast_plans=2)
+    g = torch.Generator().manual_seed(5)
+    kv = {}
+    for i, n in enumerate([30, 200, 64]):
+        k = torch.randn(n, hkv, D, generator=g).bfloat16()
+        v = torch.randn(n, hkv, D, generator=g).bfloat16()
+        be.init_request(f"r{i}", [{"key": k, "value": v}])
+        kv[f"r{i}"] = [k.float(), v.float()]
+    for step, batch in enumerate([[0], [0, 1], [0, 1, 2], [0], [0, 1, 2], [0, 1, 2], [1]]):
+        items = [{"request_id": f"r{i}", "layer_idx": 0, "score_scale": 0.09,
+                  "query": torch.randn(hq, D, generator=g),
+                  "key": torch.randn(hkv, D, generator=g).bfloat16(),
+                  "value": torch.randn(hkv, D, generator=g).bfloat16()} for i in batch]
+        res = be.decode_layer_batch(items)
+        assert len(be._fast) <= 2
+        for it, o in zip(items, res):
+            k, v = kv[it["request_id"]]
+            k = torch.cat([k, it["key"].float()[None]])
+            v = torch.cat([v, it["value"].float()[None]])
+            kv[it["request_id"]] = [k, v]
+            ref = attend(it["query"], repeat_kv(k, hq // hkv), repeat_kv(v, hq // hkv), 0.09)
+            assert_attn_close(o[0], ref, what=f"step {step} {it['request_id']}")
