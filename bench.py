@@ -354,6 +354,8 @@ def run_b200(args):
                    "num_q_heads": cfg.num_q_heads, "num_kv_heads": cfg.num_kv_heads,
                    "head_dim": cfg.head_dim, "block_size": cfg.block_size,
                    "partition_tokens": st["partition_tokens"],
+                   "split": ("balanced over all resident warps" if st["partition_tokens"] < 0
+                             else "%d-token partitions" % st["partition_tokens"]),
                    "parallelism": f"kv-head-shard{world}", "gather": gather_kind,
                    "cuda_graph": ("%d steps per graph" % args.steps) if used_graph else "none",
                    "warmup_steps_run": warm_steps,
@@ -366,7 +368,8 @@ def run_b200(args):
                      "traffic": NCU_TRAFFIC.get((args.config, world, args.kv_dtype), (None,))[0],
                      "traffic_source": NCU_TRAFFIC.get((args.config, world, args.kv_dtype),
                                                        (None, None))[1],
-                     "kernel": "paged_decode_mma_kernel + splitk_reduce_kernel",
+                     "kernel": ("paged_decode_stream_kernel" if st["partition_tokens"] < 0
+                                else "paged_decode_mma_kernel") + " + splitk_reduce_kernel",
                      "launch_ms": round(dec_ms, 5), "peak_kind": peak_kind},
         "clocks": clk,
         "gpu_launches": launches_per_step * args.steps,

@@ -44,7 +44,7 @@ from typing import Dict, List, Optional, Sequence
 import torch
 
 from . import _lib
-from .kv_cache import PagedKVPool, to_device_i32
+from .kv_cache import PagedKVPool, auto_partition, to_device_i32
 
 
 @dataclass
@@ -95,7 +95,7 @@ class _FastPlan:
         # device output and split-K workspace (per context bucket) shared by
         # this shape's graphs: they replay one after another on one stream
         self.out_dev: Optional[torch.Tensor] = None
-        self.ws: Dict[int, Optional[torch.Tensor]] = {}
+        self.ws: Dict[tuple, Optional[torch.Tensor]] = {}  # by (bucket, split)
 
 
 class _StepGraph:
@@ -286,10 +286,18 @@ class B200AttentionBackend:
         qs = [sq(it["query"]) for it in items]
         ks = [sq(it["key"]) for it in items]
         vs = [sq(it["value"]) for it in items]
-        q_dtype = qs[0].dtype
-        uniform = (all(t.dtype == q_dtype and not t.is_cuda for t in qs)
-                   and all(t.dtype == ks[0].dtype and not t.is_cuda for t in ks + vs)
-                   and q_dtype in (torch.float32, torch.float16, torch.bfloat16))
+        q_dtype, q_shape = qs[0].dtype, qs[0].shape
+        k_dtype, k_shape = ks[0].dtype, ks[0].shape
+        # the fast path gathers fixed byte counts per item: every item must have
+        # the first one's shapes and dtypes, on the host
+        uniform = q_dtype in (torch.float32, torch.float16, torch.bfloat16)
+        if uniform:
+            for t, kt, vt in zip(qs, ks, vs):
+                if (t.is_cuda or kt.is_cuda or vt.is_cuda or t.dtype != q_dtype
+                        or kt.dtype != k_dtype or vt.dtype != k_dtype or t.shape != q_shape
+                        or kt.shape != k_shape or vt.shape != k_shape):
+                    uniform = False
+                    break
         if not uniform:  # device tensors (or mixed inputs): no staging, no host sync
             out = self.decode_batch(rids, layer, torch.stack(qs), torch.stack(ks), torch.stack(vs), scale)
             if not qs[0].is_cuda:
@@ -328,7 +336,8 @@ class B200AttentionBackend:
             srcs[2 * B + i] = vt.data_ptr()
         plan.meta[:] = rows + offs + ctx_rows
         _lib.host_gather(srcs, plan.sizes, plan.n, plan.host.data_ptr())
-        step = self._step_graph(plan, layer, scale, max(targets)) if plan.warm else None
+        pt = self._split(targets, n_new)
+        step = self._step_graph(plan, layer, scale, max(targets), pt) if plan.warm else None
         if step is not None:
             # one graph launch: H2D, fused step, D2H of output and status
             step.graph.replay()
@@ -336,7 +345,7 @@ class B200AttentionBackend:
         else:
             plan.dev.copy_(plan.host, non_blocking=True)
             out = self._launch(reqs, layer, n_new, targets, plan.q, plan.k, plan.v, plan.rows,
-                               plan.offs, plan.ctx, scale, check=False)
+                               plan.offs, plan.ctx, scale, check=False, pt=pt)
             # output and status word back behind one synchronisation
             plan.out.copy_(out, non_blocking=True)
             self._status_host.copy_(self.pool.status, non_blocking=True)
@@ -351,14 +360,27 @@ class B200AttentionBackend:
     # fixed per graph, re-captured when the batch outgrows it.
     _GRAPH_CTX_BUCKET = 512
 
-    def _step_graph(self, plan: _FastPlan, layer: int, scale: float, max_ctx: int):
+    def _split(self, targets, n_new) -> int:
+        """partition_tokens for this call: the caller's, or the host's choice
+        from the batch's contexts (kv_cache.auto_partition)."""
+        if self.partition_tokens:
+            return self.partition_tokens
+        sharded = self.shard is not None and self.shard.world > 1
+        return auto_partition(targets, max(n_new), sharded)
+
+    def _step_graph(self, plan: _FastPlan, layer: int, scale: float, max_ctx: int, pt: int):
         """The captured step for this batch shape, layer, scale and context
         bucket, capturing it on first use; None where a step is not captured
         (graphs off, NCCL-gathered shards)."""
         if not self.cuda_graphs:
             return None
-        bucket = -(-max_ctx // self._GRAPH_CTX_BUCKET) * self._GRAPH_CTX_BUCKET
-        key = (layer, scale, bucket)
+        if pt < 0 and max_ctx <= self.max_seq_len:
+            # the balanced split's work follows the contexts themselves; its
+            # max_ctx_len only bounds the workspace: one bucket, no re-capture
+            bucket = self.max_seq_len
+        else:
+            bucket = -(-max_ctx // self._GRAPH_CTX_BUCKET) * self._GRAPH_CTX_BUCKET
+        key = (layer, scale, bucket, pt)
         step = plan.graphs.get(key)
         if step is not None:
             return step
@@ -380,20 +402,20 @@ class B200AttentionBackend:
         if peer is not None:
             nbytes = _lib.decode_gather_workspace_bytes(n_seqs, B, 1, bucket, q.shape[1], pool.num_kv_heads,
                                                         self.head_dim, pool.block_size, pool.dtype,
-                                                        q.dtype, self.partition_tokens)
+                                                        q.dtype, pt)
         else:
             nbytes = _lib.decode_workspace_bytes(n_seqs, B, 1, bucket, q.shape[1], pool.num_kv_heads,
                                                  self.head_dim, pool.block_size, pool.dtype, q.dtype,
-                                                 self.partition_tokens)
+                                                 pt)
         for old in [k for k in plan.graphs if k[:2] == key[:2]]:
-            del plan.graphs[old]  # an older bucket of this layer and scale
-        live = {k[2] for k in plan.graphs}
+            del plan.graphs[old]  # an older bucket (or split) of this layer and scale
+        live = {k[2:] for k in plan.graphs}
         for b in [b for b in plan.ws if b not in live]:
             del plan.ws[b]  # graphs that still use it keep their own reference
-        if bucket not in plan.ws:
-            plan.ws[bucket] = (torch.empty(nbytes, dtype=torch.uint8, device=self.device)
-                               if nbytes > 0 else None)
-        ws = plan.ws[bucket]
+        if key[2:] not in plan.ws:
+            plan.ws[key[2:]] = (torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+                                if nbytes > 0 else None)
+        ws = plan.ws[key[2:]]
         if peer is None and plan.out_dev is None:
             plan.out_dev = torch.empty_like(q)
         out_dev = None if peer is not None else plan.out_dev
@@ -405,14 +427,14 @@ class B200AttentionBackend:
                     _lib.decode_step_gather(q, pool.k[layer], pool.v[layer], k_loc, v_loc, pool.tables,
                                             plan.offs, plan.ctx, peer, max_queries_per_seq=1,
                                             max_ctx_len=bucket, score_scale=scale, seq_rows=plan.rows,
-                                            partition_tokens=self.partition_tokens, workspace=ws,
+                                            partition_tokens=pt, workspace=ws,
                                             status=pool.status)
                     src = peer.out[:B]
                 else:
                     _lib.decode_step(out_dev, q, pool.k[layer], pool.v[layer], k_loc, v_loc, pool.tables,
                                      plan.offs, plan.ctx, max_queries_per_seq=1, max_ctx_len=bucket,
                                      score_scale=scale, seq_rows=plan.rows,
-                                     partition_tokens=self.partition_tokens, workspace=ws,
+                                     partition_tokens=pt, workspace=ws,
                                      status=pool.status, check=False)
                     src = out_dev
                 plan.out.copy_(src, non_blocking=True)
@@ -477,8 +499,10 @@ class B200AttentionBackend:
         return reqs, rows, targets, offs, ctx_rows
 
     def _launch(self, reqs, layer_idx, n_new, targets, query, key, value, rows_d, offs_d, ctx_d,
-                score_scale, check: bool = True):
+                score_scale, check: bool = True, pt: Optional[int] = None):
         pool = self.pool
+        if pt is None:
+            pt = self._split(targets, n_new)
         hq = query.shape[1]
         group = hq // self.num_kv_heads
         lo, hi = self.kv_range
@@ -495,12 +519,12 @@ class B200AttentionBackend:
             # fused append + decode + reduce with the all-gather over NVLink
             out = pool.decode_step_gather(layer_idx, q, self._local_kv(key), self._local_kv(value),
                                           offs_d, ctx_d, rows_d, max(n_new), max(targets),
-                                          score_scale, peer, partition_tokens=self.partition_tokens)
+                                          score_scale, peer, partition_tokens=pt)
         else:
             # one launch: append each row's token at ctx - 1, then attend (+ reduce)
             out = pool.decode_step(layer_idx, q, self._local_kv(key), self._local_kv(value), offs_d,
                                    ctx_d, rows_d, max(n_new), max(targets), score_scale,
-                                   partition_tokens=self.partition_tokens, check=check)
+                                   partition_tokens=pt, check=check)
         self._advance(reqs, layer_idx, n_new, targets)
         if sharded and peer is None:
             out = self.shard.gather(out, self.num_kv_heads, group)

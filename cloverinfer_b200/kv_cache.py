@@ -37,6 +37,20 @@ def to_device_i32(values: Sequence[int], device: torch.device) -> torch.Tensor:
     return h.pin_memory().to(device, non_blocking=True)
 
 
+def auto_partition(contexts: Sequence[int], max_q: int, sharded: bool = False) -> int:
+    """The split for a batch whose caller left it to the library (0): the
+    balanced split (``_lib.PARTITION_BALANCED``) for ragged batches of
+    single-token rows — the longest context at least 1.25x the mean, where
+    fixed partitions sized for the longest leave most CTAs short or empty —
+    else 0 (fixed partitions chosen by the library from the longest context).
+    Sharded steps keep 0."""
+    n = len(contexts)
+    if sharded or max_q != 1 or n == 0 or n > 1024:
+        return 0
+    longest = max(contexts)
+    return _lib.PARTITION_BALANCED if longest * n >= 1.25 * sum(contexts) and longest > 0 else 0
+
+
 class PagedKVPool:
     def __init__(self, num_blocks: int, block_size: int, num_kv_heads: int, head_dim: int, *,
                  num_layers: int = 1, dtype: torch.dtype = torch.bfloat16,

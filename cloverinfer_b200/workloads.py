@@ -107,7 +107,7 @@ def build_decode_step(cfg, rank, world, lens, device, seed=0, gather=None, n_new
     fixed partition length on one GPU (the library's choice on several)."""
     from . import _lib
     from .head_groups import kv_head_shards
-    from .kv_cache import PagedKVPool
+    from .kv_cache import PagedKVPool, auto_partition
 
     lo, hi = kv_head_shards(cfg.num_kv_heads, world)[rank]
     hkv_l = hi - lo
@@ -131,6 +131,8 @@ def build_decode_step(cfg, rank, world, lens, device, seed=0, gather=None, n_new
     pt = partition_tokens
     if pt is None:
         pt = cfg.partition_tokens if world == 1 else 0
+    if pt == 0:
+        pt = auto_partition(lens, max(n_new), world > 1)
     pt = _lib.decode_partition_tokens(B, T, max_q, max(lens), hq_l, hkv_l, D, bs, dt, torch.float32, pt)
     if pt == 0:
         pt = _lib.PARTITION_BALANCED  # the library took the balanced split

@@ -9,6 +9,7 @@ cross a context bucket, so a graph is re-captured mid-run.
 
 from __future__ import annotations
 
+import pytest
 import torch
 
 from conftest import assert_attn_close, gpu
@@ -92,3 +93,20 @@ def test_plan_cache_is_bounded_and_stays_correct():
             kv[it["request_id"]] = [k, v]
             ref = attend(it["query"], repeat_kv(k, hq // hkv), repeat_kv(v, hq // hkv), 0.09)
             assert_attn_close(o[0], ref, what=f"step {step} {it['request_id']}")
+
+
+def test_mismatched_item_shapes_raise():
+    """Items whose query/key shapes differ cannot share the fixed-size host
+    gather: the call raises instead of reading past a smaller tensor."""
+    from cloverinfer_b200 import B200AttentionBackend
+    be = B200AttentionBackend(num_blocks=64, block_size=16, num_kv_heads=2,
+                              kv_dtype=torch.bfloat16, device="cuda", max_seqs=4)
+    for rid in ("a", "b"):
+        be.init_request(rid, [{"key": torch.randn(20, 2, 64).bfloat16(),
+                               "value": torch.randn(20, 2, 64).bfloat16()}])
+    items = [{"request_id": "a", "layer_idx": 0, "query": torch.randn(8, 64),
+              "key": torch.randn(2, 64).bfloat16(), "value": torch.randn(2, 64).bfloat16()},
+             {"request_id": "b", "layer_idx": 0, "query": torch.randn(4, 64),
+              "key": torch.randn(2, 64).bfloat16(), "value": torch.randn(2, 64).bfloat16()}]
+    with pytest.raises(Exception):
+        be.decode_layer_batch(items)
