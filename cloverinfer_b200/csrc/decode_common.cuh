@@ -167,7 +167,6 @@ struct MmaGeom {
   static constexpr int kCols = kMmaCols * NT;  // columns per warp (NT n-tiles)
   static constexpr int kRedBytes = kMmaWarps * kCols * (D + 4) * 4 + 2 * kMmaWarps * kCols * 4;
   static constexpr int kSmem = (kPipeBytes > kRedBytes ? kPipeBytes : kRedBytes) + 1024;
-  static constexpr int kMaxGroupsPerWarp = 32;  // one lane holds the block ids of one group
 };
 
 // byte offset of 16-byte chunk `cg` (along head_dim) of stage row `r`
