@@ -988,6 +988,13 @@ static int make_plan(int n_seqs, int n_rows, int max_q, int max_ctx, int hq, int
   return CLOVER_B200_OK;
 }
 
+// The sharded step (decode + the reduce with the NVLink all-gather) runs on
+// fixed partitions: a request for the balanced split becomes the library's
+// fixed-partition choice there.
+static int gather_partition(int partition_tokens) {
+  return partition_tokens == CLOVER_B200_PARTITION_BALANCED ? 0 : partition_tokens;
+}
+
 }  // namespace clover
 
 using namespace clover;
@@ -1233,7 +1240,8 @@ extern "C" int64_t clover_b200_decode_gather_workspace_bytes(
     int32_t kv_dtype, int32_t q_dtype, int32_t partition_tokens) {
   DecodePlan pl;
   if (make_plan(n_seqs, n_query_rows, max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads,
-                head_dim, block_size, kv_dtype, q_dtype, partition_tokens, &pl) != CLOVER_B200_OK)
+                head_dim, block_size, kv_dtype, q_dtype, gather_partition(partition_tokens),
+                &pl) != CLOVER_B200_OK)
     return -1;
   return pl.gather_workspace_bytes;
 }
@@ -1268,6 +1276,6 @@ extern "C" int clover_b200_decode_step_gather(
                      num_blocks, block_size, k_new, v_new, new_token_stride, block_tables,
                      table_stride, seq_rows, query_start_loc, ctx_lens, n_seqs, n_query_rows,
                      max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads, head_dim,
-                     score_scale, partition_tokens, workspace, workspace_bytes_, dev_status, stream,
+                     score_scale, gather_partition(partition_tokens), workspace, workspace_bytes_, dev_status, stream,
                      &g);
 }

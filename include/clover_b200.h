@@ -149,8 +149,9 @@ CLOVER_B200_API int clover_b200_kv_append(void* k_cache, void* v_cache, const vo
  * split on the tensor-core path (bf16/fp16 cache, head_dim 64/128/256, block
  * 16/32, at most 1024 sequences): the KV blocks of all sequences are divided
  * evenly over every resident warp instead of into fixed-length partitions, so
- * ragged batches launch no empty work.  Elsewhere it means the library's
- * choice (as 0).
+ * ragged batches launch no empty work.  Elsewhere, and for the sharded step
+ * (clover_b200_decode_step_gather and its workspace query), it means the
+ * library's choice (as 0).
  */
 #define CLOVER_B200_PARTITION_BALANCED (-1)
 
