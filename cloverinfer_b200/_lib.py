@@ -44,6 +44,7 @@ _F = ctypes.c_float
 SIGNATURES = {
     "clover_b200_version": (ctypes.c_int, []),
     "clover_b200_last_error": (ctypes.c_char_p, []),
+    "clover_b200_set_wait_limit_ns": (ctypes.c_int64, [_I64]),
     "clover_b200_host_gather": (ctypes.c_int, [_P, _P, _I32, _P]),
     "clover_b200_block_reserve": (ctypes.c_int, [_P, _P, _I32, _P, _I32, _P, _P, _P, _I32, _I32, _P, _P]),
     "clover_b200_block_free": (ctypes.c_int, [_P, _P, _I32, _P, _I32, _P, _P, _I32, _P, _P]),
@@ -356,6 +357,12 @@ def decode_step_gather(q, k_cache, v_cache, k_new, v_new, block_tables, query_st
         gather.peer_recv_d.data_ptr(), gather.sync.data_ptr(), gather.world, gather.rank,
         gather.half_words, _ptr(workspace), ws_bytes, _ptr(status), _stream(q.device))
     _check(rc, "clover_b200_decode_step_gather")
+
+
+def set_wait_limit_ns(ns: int) -> int:
+    """Limit of the kernels' bounded waits for later launches (<= 0: the 1 s
+    default); returns the previous limit."""
+    return int(lib().clover_b200_set_wait_limit_ns(int(ns)))
 
 
 def host_gather(srcs, sizes, n: int, dst_ptr: int) -> None:

@@ -374,9 +374,11 @@ class B200AttentionBackend:
         (graphs off, NCCL-gathered shards)."""
         if not self.cuda_graphs:
             return None
-        if pt < 0 and max_ctx <= self.max_seq_len:
+        sharded = self.shard is not None and self.shard.world > 1
+        if pt < 0 and not sharded and max_ctx <= self.max_seq_len:
             # the balanced split's work follows the contexts themselves; its
-            # max_ctx_len only bounds the workspace: one bucket, no re-capture
+            # max_ctx_len only bounds the workspace: one bucket, no re-capture.
+            # (A sharded step runs fixed partitions, sized by the bucket.)
             bucket = self.max_seq_len
         else:
             bucket = -(-max_ctx // self._GRAPH_CTX_BUCKET) * self._GRAPH_CTX_BUCKET
@@ -385,7 +387,6 @@ class B200AttentionBackend:
         if step is not None:
             return step
         pool = self.pool
-        sharded = self.shard is not None and self.shard.world > 1
         group = plan.q.shape[1] // self.num_kv_heads
         lo, hi = self.kv_range
         q = plan.q if q_local_is_whole(lo, hi, self.num_kv_heads) else plan.q[:, lo * group:hi * group]

@@ -1,4 +1,5 @@
 // Library-wide C ABI pieces: version, last-error string, CUDA error mapping.
+#include <atomic>
 #include <stdarg.h>
 #include <stdio.h>
 #include <string.h>
@@ -22,6 +23,10 @@ int check_cuda(cudaError_t e, const char* what) {
   return set_error(CLOVER_B200_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
+static std::atomic<int64_t> g_wait_ns{(int64_t)kWaitLimitNs};
+
+uint64_t wait_limit_ns() { return (uint64_t)g_wait_ns.load(std::memory_order_relaxed); }
+
 }  // namespace clover
 
 extern "C" int clover_b200_version(void) { return 100; }  // 0.1.0
@@ -43,3 +48,11 @@ extern "C" int clover_b200_host_gather(const void* const* srcs, const int64_t* n
 }
 
 extern "C" const char* clover_b200_last_error(void) { return clover::g_last_error; }
+
+extern "C" int64_t clover_b200_set_wait_limit_ns(int64_t ns) {
+  constexpr int64_t kMin = 1000ll * 1000ll;             // 1 ms
+  constexpr int64_t kMax = 60ll * 1000ll * 1000ll * 1000ll;  // 60 s
+  if (ns <= 0) ns = (int64_t)clover::kWaitLimitNs;
+  ns = ns < kMin ? kMin : (ns > kMax ? kMax : ns);
+  return clover::g_wait_ns.exchange(ns);
+}

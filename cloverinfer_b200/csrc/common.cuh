@@ -19,6 +19,9 @@ namespace clover {
 // Thread-local last-error string (clover_b200_last_error) and a setter.
 int set_error(int code, const char* fmt, ...);
 int check_cuda(cudaError_t e, const char* what);
+// Limit of the kernels' bounded waits for launches made now
+// (clover_b200_set_wait_limit_ns; 1 s by default).
+uint64_t wait_limit_ns();
 
 // ---------------------------------------------------------------- device side
 __device__ __forceinline__ void raise_status(int32_t* status, int32_t bits) {
@@ -226,6 +229,8 @@ __device__ __forceinline__ void store_f<__nv_bfloat16>(__nv_bfloat16* p, float x
   *p = __float2bfloat16_rn(x);
 }
 
+// Default limit of a bounded wait, and the fixed limit of the drain of a
+// warp's own copies in flight after a wait gave up (those copies always land).
 constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
 
 }  // namespace clover

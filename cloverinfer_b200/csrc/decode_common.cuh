@@ -85,6 +85,8 @@ struct DecodeArgs {
   int32_t max_q;
   int32_t min_units;
   int32_t* part_count;
+  // Limit of this launch's bounded waits (wait_limit_ns() at launch).
+  uint64_t wait_ns;
 };
 
 // Fused output all-gather over peer memory, LL style: every value travels as

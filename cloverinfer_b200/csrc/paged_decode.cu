@@ -337,7 +337,7 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
 
   for (int k = 0; k < n_mine; ++k) {
     const int s = k % STAGES;
-    if (!mbar_wait_bounded(bar0 + s * 8, (k / STAGES) & 1, kWaitLimitNs)) {
+    if (!mbar_wait_bounded(bar0 + s * 8, (k / STAGES) & 1, a.wait_ns)) {
       timed_out = true;
       break;
     }
@@ -678,7 +678,7 @@ reduce_gather_kernel(const DecodeArgs a, const GatherArgs g, int D) {
       const uint64_t* src = g.peer_ll[g.rank] + half + ((int64_t)r * g.total_q_heads + head) * D + dim;
       uint64_t w = ld_relaxed_sys_u64(src);
       while ((uint32_t)(w >> 32) != (uint32_t)epoch && !timed_out) {
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (global_timer_ns() - t0 > a.wait_ns) {
           timed_out = true;
           break;
         }
@@ -1104,6 +1104,7 @@ static int decode_impl(
   a.max_q = max_queries_per_seq > 0 ? max_queries_per_seq : 1;
   a.min_units = kStreamMinUnits;
   a.part_count = nullptr;
+  a.wait_ns = wait_limit_ns();
   if (pl.stream) {
     // Stream workspace: partials, their log-sum-exp, then the part counts.
     a.part_tokens = block_size;

@@ -63,10 +63,16 @@ extern "C" int clover_b200_paged_decode_noalloc(
     int32_t n_seqs, int32_t n_query_rows, int32_t max_queries_per_seq, int32_t max_ctx_len,
     int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, float score_scale,
     int32_t partition_tokens, int32_t* dev_status, void* stream) {
+  // The plan query returns the same code (and message) clover_b200_paged_decode
+  // would for these sizes (invalid sizes, or an unsupported dtype / shape).
+  const int plan_rc = clover_b200_decode_partition_tokens(
+      n_seqs, n_query_rows, max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads, head_dim,
+      block_size, kv_dtype, q_dtype, partition_tokens);
+  if (plan_rc < 0) return plan_rc;
   const int64_t need = clover_b200_decode_workspace_bytes(
       n_seqs, n_query_rows, max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads, head_dim,
       block_size, kv_dtype, q_dtype, partition_tokens);
-  if (need < 0) return CLOVER_B200_ERR_INVALID_ARG;  // message set by the size check
+  if (need < 0) return CLOVER_B200_ERR_INVALID_ARG;  // unreachable once the plan query passed
   if (need > (int64_t)CLOVER_B200_NOALLOC_SCRATCH_BYTES)
     return set_error(CLOVER_B200_ERR_WORKSPACE,
                      "paged_decode_noalloc: split-K scratch of %lld bytes exceeds the static "

@@ -411,7 +411,7 @@ paged_decode_stream_kernel(const __grid_constant__ CUtensorMap tmK,
   bool timed_out = false;
   for (int k = 0; k < n_units; ++k) {
     const int s = k % STAGES;
-    if (!mbar_wait_bounded(bar0 + s * 8, (k / STAGES) & 1, kWaitLimitNs)) {
+    if (!mbar_wait_bounded(bar0 + s * 8, (k / STAGES) & 1, a.wait_ns)) {
       timed_out = true;
       break;
     }

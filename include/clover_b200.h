@@ -11,7 +11,10 @@
  * Conventions
  *   - Plain device pointers and sizes; no framework types.  All memory is
  *     caller-owned (the caller allocates caches, tables, outputs and the
- *     split-K workspace).  Nothing in this header allocates device memory.
+ *     split-K workspace).  The one entry point that allocates device memory
+ *     is clover_b200_ipc_alloc, the set-up of a fused-gather receive buffer
+ *     (cudaMalloc, so that peers can map it with CUDA IPC); no decode, append
+ *     or allocator call allocates.
  *   - Every entry point returns CLOVER_B200_OK (0) or a negative
  *     CLOVER_B200_ERR_* code and never throws; clover_b200_last_error()
  *     returns a thread-local description of the last failure.
@@ -72,6 +75,20 @@ CLOVER_B200_API int clover_b200_version(void);
 
 /* Thread-local description of the last error returned on this thread. */
 CLOVER_B200_API const char* clover_b200_last_error(void);
+
+/*
+ * Limit, in nanoseconds, of the kernels' bounded waits: a TMA copy that has
+ * not landed, and the fused gather's wait for the other ranks' words.  When a
+ * wait runs out the kernel sets CLOVER_B200_DEV_TIMEOUT in *dev_status and
+ * returns (missing gathered values read as 0; later CTAs exit at once until
+ * the caller clears the word).  Process-wide; applies to launches made after
+ * the call (a captured graph keeps the limit it was captured with).  ns <= 0
+ * restores the default of 1 s; values are clamped to [1 ms, 60 s].  Returns
+ * the previous limit.  No counterpart in the reference, whose kernels never
+ * wait; it bounds how long a rank waits for a peer that failed, the device
+ * side of AttentionNode's surfaced errors (src/core/nodes.py:167-170).
+ */
+CLOVER_B200_API int64_t clover_b200_set_wait_limit_ns(int64_t ns);
 
 /*
  * Host helper: copy n host buffers back to back into dst (a pinned staging

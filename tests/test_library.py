@@ -64,3 +64,44 @@ def test_sources_target_sm100a_only():
              if f.endswith((".cu", ".cuh"))]
     srcs = "".join(open(p).read() for p in files)
     assert "cp.async.bulk.tensor" in srcs and "mma.sync" in srcs
+
+
+def test_no_alloc_reports_the_plan_error():
+    """The allocation-free decode returns the code the regular entry point
+    returns for the same unsupported request (an fp8 cache at head_dim 64),
+    not a generic invalid-argument code.  No GPU work is issued."""
+    lib = _lib.lib()
+    args = (None, 0, None, 0, _lib.F32, None, None, _lib.FP8_E4M3, 1, 16, None, 1, None, None, None,
+            1, 1, 1, 4096, 8, 2, 64, 1.0, 0)
+    rc = lib.clover_b200_paged_decode(*args, None, 0, None, None)
+    assert rc == _lib.ERR_UNSUPPORTED
+    rc2 = lib.clover_b200_paged_decode_noalloc(*args, None, None)
+    assert rc2 == rc
+    assert b"fp8" in lib.clover_b200_last_error()
+
+
+def test_wait_limit_setter_round_trips():
+    lib = _lib.lib()
+    prev = _lib.set_wait_limit_ns(5_000_000)
+    try:
+        assert _lib.set_wait_limit_ns(1) == 5_000_000      # clamped up to 1 ms next
+        assert _lib.set_wait_limit_ns(0) == 1_000_000      # 0 restores the default
+        assert _lib.set_wait_limit_ns(10 ** 15) == 1_000_000_000
+        assert lib.clover_b200_set_wait_limit_ns(prev) == 60 * 10 ** 9
+    finally:
+        _lib.set_wait_limit_ns(prev)
+
+
+def test_clover_kernels_shim_rejects_bad_shapes_on_cpu():
+    """The clover_kernels stand-in validates arguments before any GPU work."""
+    import pytest
+    import torch
+    from cloverinfer_b200 import clover_kernels
+    q = torch.zeros(2, 4, 32)
+    kc = torch.zeros(8, 16, 4, 32)
+    with pytest.raises(ValueError):
+        clover_kernels.paged_attention(torch.zeros(3, 4, 32), q, kc, kc, torch.zeros(2, 1, dtype=torch.int32),
+                                       torch.ones(2, dtype=torch.int32), 16, 1)
+    with pytest.raises(ValueError):
+        clover_kernels.paged_attention(torch.zeros_like(q), q, kc, kc, torch.zeros(2, 1, dtype=torch.int32),
+                                       torch.ones(2, dtype=torch.int32), 8, 1)

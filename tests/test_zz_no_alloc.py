@@ -44,11 +44,13 @@ def _case(seed, lens, hq=32, hkv=8, D=128, bs=16, dt=torch.bfloat16):
 
 
 def _with_workspace(c, pt):
+    """The regular entry point with a fresh workspace filled with NaN bytes, so
+    a partial that a call forgets to write cannot pass for a correct one."""
     from cloverinfer_b200 import _lib
     out = torch.empty_like(c["q"])
     need = _lib.decode_workspace_bytes(len(c["lens"]), len(c["lens"]), 1, max(c["lens"]), c["hq"],
                                        c["hkv"], c["D"], c["bs"], c["dt"], c["q"].dtype, pt)
-    ws = torch.empty(max(need, 1), dtype=torch.uint8, device="cuda")
+    ws = torch.full((max(need, 1),), 255, dtype=torch.uint8, device="cuda")
     st = torch.zeros(1, dtype=torch.int32, device="cuda")
     _lib.paged_decode(out, c["q"], c["kc"], c["vc"], c["tables"], c["qsl"], c["ctx"],
                       max_queries_per_seq=1, max_ctx_len=max(c["lens"]),
@@ -83,6 +85,23 @@ def test_no_alloc_matches_workspace_entry_point_twice():
         assert rc == _lib.OK, _lib.lib().clover_b200_last_error()
         assert st == 0
         assert_attn_close(out, ref, kv_dtype=torch.bfloat16, what=f"no-alloc vs workspace pt={pt}")
+
+
+def test_no_alloc_balanced_split_twice():
+    """The balanced split keeps per-(row, head) part counts in the shared array
+    too: a second, more ragged call with fewer rows and an empty context must
+    not read the first call's counts or partials."""
+    from cloverinfer_b200 import _lib
+    first = _case(3, [4096, 1500, 700, 33, 2600, 9000, 64, 512])
+    second = _case(4, [0, 40, 16000, 17, 3000])
+    for c in (first, second):
+        ref = _with_workspace(c, _lib.PARTITION_BALANCED)
+        rc, out, st = _no_alloc(c, _lib.PARTITION_BALANCED)
+        assert rc == _lib.OK, _lib.lib().clover_b200_last_error()
+        assert st == 0
+        if c is second:
+            assert bool((out[0] == 0).all())  # the empty context reads 0
+        assert_attn_close(out, ref, kv_dtype=torch.bfloat16, what="no-alloc vs workspace, balanced")
 
 
 def test_no_alloc_rejects_oversized_scratch():
