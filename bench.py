@@ -20,6 +20,18 @@ read per step (sum_s ctx_s * Hkv * D * 2 * elem) / step time, whole job.
 ``--impl reference`` times the CPU reference implementation (the oracle port
 of CloverInfer's CpuAttentionBackend, all host threads) on a bounded sample of
 the same workload and prints the same metric.
+
+After the timed region every rank runs one more (untimed) step and checks the
+all-gathered output of EVERY row and head against a plain torch fp32 attention
+over the same cache contents (and the appended K/V bit for bit); the worst
+error over all ranks is the line's ``parity``.  ``spread`` holds the per-step
+times of 30 further, individually timed graph replays, and ``as_configured``
+the same measurement with the configuration's own partition length (512
+tokens for c3) next to the library's choice.
+
+``--profile-share W`` is the ncu case for one rank of a W-way KV-head shard:
+it builds rank ``--profile-rank`` 's share of the step on one GPU and launches
+the decode (+ split-K reduce) ``--launches`` times, printing no JSON.
 """
 
 from __future__ import annotations
@@ -219,14 +231,162 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------ B200 arm
-def build_step(cfg, rank, world, lens, device, seed=0, gather=None, n_new=None):
+def build_step(cfg, rank, world, lens, device, seed=0, gather=None, n_new=None, partition_tokens=0):
     from cloverinfer_b200.workloads import build_decode_step
-    return build_decode_step(cfg, rank, world, lens, device, seed=seed, gather=gather, n_new=n_new)
+    return build_decode_step(cfg, rank, world, lens, device, seed=seed, gather=gather, n_new=n_new,
+                             partition_tokens=partition_tokens)
+
+
+def _replay_ms(graph, stream, replays: int, steps: int):
+    """Per-step ms of `replays` individually timed replays of a `steps`-step graph."""
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(replays)]
+    with torch.cuda.stream(stream):
+        for e0, e1 in evs:
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) / steps for a, b in evs]
+
+
+def _spread(ms):
+    s = sorted(ms)
+    pick = lambda f: s[min(len(s) - 1, max(0, int(round(f * (len(s) - 1)))))]  # noqa: E731
+    return {"replays": len(s), "median_ms": round(statistics.median(s), 5),
+            "p10_ms": round(pick(0.1), 5), "p90_ms": round(pick(0.9), 5)}
+
+
+def _bits(t: torch.Tensor) -> torch.Tensor:
+    return t.view({1: torch.uint8, 2: torch.int16, 4: torch.int32}[t.element_size()])
+
+
+def reference_step(cfg, st, lens, device):
+    """This rank's heads of the step, recomputed with plain torch fp32
+    attention over the cache as the step left it: row r of sequence b attends
+    to its first ctx_r tokens (softmax(scale q.K^T).V, the math of
+    CpuAttentionBackend.decode_layer, src/core/attention_backend.py:113-118).
+    Also counts appended tokens whose cached K or V differ, bit for bit, from
+    the step's new K/V.  Returns ([T, Hq_local, D] fp32, mismatches)."""
+    pool, q = st["pool"], st["q"]
+    hq_l, hkv_l, D, bs = st["hq_local"], st["hkv_local"], cfg.head_dim, cfg.block_size
+    grp = hq_l // hkv_l
+    K = pool.k[0].view(-1, hkv_l, D)
+    V = pool.v[0].view(-1, hkv_l, D)
+    T = q.shape[0]
+    ref = torch.empty((T, hq_l, D), dtype=torch.float32, device=device)
+    ctx = torch.tensor(st["ctx_rows"], dtype=torch.int64, device=device)
+    lane = torch.arange(bs, device=device)
+    mism = torch.zeros((), dtype=torch.int64, device=device)
+    r = 0
+    for b, (n, k) in enumerate(zip(lens, st["n_new"])):
+        blocks = pool.tables[b, :-(-n // bs)].long()
+        slots = (blocks[:, None] * bs + lane).reshape(-1)[:n]
+        new = slots[n - k:]
+        mism += (_bits(K[new]) != _bits(st["k_new"][r:r + k])).flatten(1).any(1).sum()
+        mism += (_bits(V[new]) != _bits(st["v_new"][r:r + k])).flatten(1).any(1).sum()
+        kb, vb = K[slots].float(), V[slots].float()
+        qb = q[r:r + k].float().view(k, hkv_l, grp, D)
+        s = torch.einsum("jhgd,lhd->jhgl", qb, kb) * cfg.score_scale
+        masked = torch.arange(n, device=device)[None, :] >= ctx[r:r + k, None]
+        s.masked_fill_(masked[:, None, None, :], float("-inf"))
+        ref[r:r + k] = torch.einsum("jhgl,lhd->jhgd", torch.softmax(s, dim=-1), vb).reshape(k, hq_l, D)
+        r += k
+    return ref, int(mism)
+
+
+def check_parity(cfg, st, lens, world, device, gathered):
+    """Worst error of the gathered [T, Hq, D] output (every row and head) on
+    every rank against the torch fp32 reference of all ranks' heads; same
+    collective sequence on every rank, errors included."""
+    err = [float("nan"), float("nan"), 0.0, 0.0]
+    ref_local = None
+    try:
+        ref_local, mism = reference_step(cfg, st, lens, device)
+        err[2] = float(mism)
+    except Exception as e:  # keep the collectives in step; report the failure
+        print(f"parity reference failed: {e!r}", file=sys.stderr)
+        err[2] = -1.0
+    T, hq_l, D = st["rows"], st["hq_local"], cfg.head_dim
+    if ref_local is None:
+        ref_local = torch.zeros((T, hq_l, D), dtype=torch.float32, device=device)
+    if world > 1:
+        import torch.distributed as dist
+        allr = torch.empty((world * T, hq_l, D), dtype=torch.float32, device=device)
+        dist.all_gather_into_tensor(allr, ref_local.contiguous())
+        ref = allr.view(world, T, hq_l, D).permute(1, 0, 2, 3).reshape(T, world * hq_l, D)
+    else:
+        ref = ref_local
+    if err[2] >= 0:
+        o = gathered.float()
+        e = (o - ref).abs()
+        err[0] = float(e.max())
+        err[1] = float((e / ref.abs().clamp_min(1e-3)).max())
+        err[3] = float((~torch.isfinite(o)).sum())
+    t = torch.tensor(err, dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    max_abs, max_rel, mism, nonfinite = (float(x) for x in t.tolist())
+    ok = (mism == 0 and nonfinite == 0 and max_abs <= 2e-3 and max_rel <= 1e-2)
+    return {"max_abs": max_abs, "max_rel": max_rel, "rows_checked": T,
+            "heads_checked": cfg.num_q_heads, "append_mismatches": int(mism),
+            "nonfinite": int(nonfinite), "pass": bool(ok),
+            "reference": "torch fp32 attention over the cache contents, all rows and heads, "
+                         "checked on every rank (worst rank reported); appended K/V bit-exact",
+            "tolerance": {"max_abs": 2e-3, "max_rel_floored": 1e-2}}
+
+
+def run_profile_share(args):
+    """One rank's share of a W-way sharded step on one GPU, decode (+ reduce)
+    launched --launches times: the case ncu captures for a multi-GPU rank."""
+    from cloverinfer_b200.workloads import build_decode_step, context_lengths, new_tokens
+    cfg = config_for(args)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lens = context_lengths(cfg, 0, args.batch)
+    pt = args.partition_tokens if args.partition_tokens is not None else 0
+    st = build_decode_step(cfg, args.profile_rank, args.profile_share, lens, dev,
+                           n_new=new_tokens(cfg, 0, args.batch), partition_tokens=pt)
+    for _ in range(args.launches):
+        st["decode_only"]()
+    torch.cuda.synchronize()
+    st["pool"].check_status()
+    print(f"{cfg.name}: rank {args.profile_rank}/{args.profile_share}, {st['hkv_local']} KV heads, "
+          f"partition {st['partition_tokens']} tokens, {args.launches} launches ok")
+
+
+def _step_runner(st, world, T, cfg, device):
+    """The full step of a built workload (the step, plus an NCCL all-gather
+    when the fused peer gather is not in use) and a function returning the
+    gathered [T, Hq, D] output the last step left."""
+    peer = st.get("peer")
+    if world == 1:
+        return st["step"], lambda: st["out"]
+    if peer is not None:
+        return st["step"], lambda: peer.out[:T]
+    import torch.distributed as dist
+    hq_l, D = st["hq_local"], cfg.head_dim
+    recv = torch.empty((world * T, hq_l, D), dtype=st["out"].dtype, device=device)
+
+    def full_step():
+        st["step"]()
+        dist.all_gather_into_tensor(recv, st["out"])
+
+    return full_step, lambda: recv.view(world, T, hq_l, D).permute(1, 0, 2, 3).reshape(T, world * hq_l, D)
+
+
+def _capture(fn, steps, stream):
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for _ in range(steps):
+            fn()
+    return g
 
 
 def run_b200(args):
     from cloverinfer_b200 import _lib
-    from cloverinfer_b200.workloads import CONFIGS, context_lengths, kv_bytes, new_tokens
+    from cloverinfer_b200.workloads import kv_bytes, new_tokens, context_lengths
 
     rank, world, local = _dist_setup()
     device = torch.device("cuda", local)
@@ -240,29 +400,18 @@ def run_b200(args):
     total_kv = kv_bytes(lens, cfg.num_kv_heads, cfg.head_dim, cfg.dtype)
     peer = None
     if world > 1 and args.gather == "peer":
-        from cloverinfer_b200.head_groups import kv_head_shards
         from cloverinfer_b200.sharded import HeadShardGroup, PeerGather
-        lo, hi = kv_head_shards(cfg.num_kv_heads, world)[rank]
         peer = PeerGather(HeadShardGroup(), T, cfg.num_q_heads, cfg.head_dim, torch.float32, device)
-    st = build_step(cfg, rank, world, lens, device, gather=peer, n_new=n_new)
+    pt_arg = args.partition_tokens if args.partition_tokens is not None else 0
+    st = build_step(cfg, rank, world, lens, device, gather=peer, n_new=n_new, partition_tokens=pt_arg)
+    st["peer"] = peer
     local_kv = kv_bytes(lens, st["hkv_local"], cfg.head_dim, cfg.dtype)
-    gather = None
-    if world > 1 and peer is None:
-        import torch.distributed as dist
-        recv = torch.empty((world * T, st["hq_local"], cfg.head_dim), dtype=st["out"].dtype, device=device)
-
-        def gather():
-            dist.all_gather_into_tensor(recv, st["out"])
+    full_step, gathered = _step_runner(st, world, T, cfg, device)
 
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
-    launches_per_step = 1 + (1 if st["workspace_bytes"] > 0 else 0)
+    launches_per_step = 1 + (1 if st["workspace_bytes"] > 0 or peer is not None else 0)
     gather_kind = "none" if world == 1 else ("fused-peer-stores" if peer is not None else "nccl")
-
-    def full_step():
-        st["step"]()
-        if gather is not None:
-            gather()
 
     with torch.cuda.stream(stream):
         for _ in range(3):  # eager warm-up (module load, tensor maps, NCCL comm init)
@@ -272,12 +421,7 @@ def run_b200(args):
     # steps, and programmatic dependent launch between a step's reduce and the
     # next step's decode.  The warm-up replays the same graph (its first launch
     # also uploads it), so at least W steps run untimed.
-    graph = None
-    if not args.no_graph:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for _ in range(args.steps):
-                full_step()
+    graph = None if args.no_graph else _capture(full_step, args.steps, stream)
     warm_replays = -(-args.warmup // args.steps)
     warm_steps = warm_replays * args.steps if graph is not None else args.warmup
 
@@ -311,22 +455,22 @@ def run_b200(args):
     ms = e0.elapsed_time(e1) / args.steps
     ms = _max_over_ranks(ms, world)
 
+    # Spread: further replays of the same graph, each timed on its own.
+    spread = None
+    if graph is not None:
+        _barrier(world)
+        reps = _replay_ms(graph, stream, args.replays, args.steps)
+        spread = _spread([_max_over_ranks(x, world) for x in reps])
+
     # Dominant kernel alone: decode (+ its split-K reduce) launches back to back
-    # in one graph, timed between CUDA events on the launching stream.
-    dec_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(dec_graph, stream=stream):
-        for _ in range(args.steps):
-            st["decode_only"]()
+    # in one graph, timed between CUDA events on the launching stream (median
+    # of the individually timed replays).
+    dec_graph = _capture(st["decode_only"], args.steps, stream)
     with torch.cuda.stream(stream):
         dec_graph.replay()
-        torch.cuda.synchronize(device)
-        d0 = torch.cuda.Event(enable_timing=True)
-        d1 = torch.cuda.Event(enable_timing=True)
-        d0.record(stream)
-        dec_graph.replay()
-        d1.record(stream)
     torch.cuda.synchronize(device)
-    dec_ms = d0.elapsed_time(d1) / args.steps
+    dec_reps = _replay_ms(dec_graph, stream, args.replays, args.steps)
+    dec_ms = statistics.median(dec_reps)
     clk = clocks.stop()
     st["pool"].check_status()
     used_graph = graph is not None
@@ -337,6 +481,46 @@ def run_b200(args):
     dec_graph.reset()
     del graph, dec_graph
     torch.cuda.synchronize(device)
+
+    # Parity: one more step, then every row and head against torch fp32.
+    with torch.cuda.stream(stream):
+        full_step()
+    torch.cuda.synchronize(device)
+    st["pool"].check_status()
+    parity = check_parity(cfg, st, lens, world, device, gathered())
+
+    # The configuration's own partition length next to the library's choice.
+    as_cfg = None
+    if cfg.partition_tokens and not args.no_graph and cfg.partition_tokens != st["partition_tokens"]:
+        st2 = build_step(cfg, rank, world, lens, device, gather=peer, n_new=n_new,
+                         partition_tokens=cfg.partition_tokens)
+        st2["peer"] = peer
+        step2, gathered2 = _step_runner(st2, world, T, cfg, device)
+        with torch.cuda.stream(stream):
+            step2()
+        torch.cuda.synchronize(device)
+        g2 = _capture(step2, args.steps, stream)
+        with torch.cuda.stream(stream):
+            for _ in range(warm_replays):
+                g2.replay()
+        torch.cuda.synchronize(device)
+        _barrier(world)
+        reps2 = [_max_over_ranks(x, world) for x in _replay_ms(g2, stream, args.replays, args.steps)]
+        g2.reset()
+        del g2
+        torch.cuda.synchronize(device)
+        st2["pool"].check_status()
+        with torch.cuda.stream(stream):
+            step2()
+        torch.cuda.synchronize(device)
+        par2 = check_parity(cfg, st2, lens, world, device, gathered2())
+        med2 = statistics.median(reps2)
+        as_cfg = {"partition_tokens": st2["partition_tokens"],
+                  "value": round(total_kv / (med2 * 1e-3) / 1e9, 2), "unit": "GB/s",
+                  "ms_per_step": round(med2, 5), "spread": _spread(reps2),
+                  "parity": {k: par2[k] for k in ("max_abs", "max_rel", "pass")}}
+        del st2
+        torch.cuda.empty_cache()
 
     # ---------------- e2e through the public API (host buffers in, host out)
     e2e = run_e2e(cfg, lens, n_new, rank, world, device, args)
@@ -363,6 +547,9 @@ def run_b200(args):
         "steps_per_s": round(1e3 / ms, 2),
         "tokens_per_s": round(T * 1e3 / ms, 2),
         "pct_hbm_peak_per_gpu": round(100.0 * value / world / hbm_peak, 2),
+        "spread": spread,
+        "parity": parity,
+        "as_configured": as_cfg,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4),
                      "traffic": NCU_TRAFFIC.get((args.config, world, args.kv_dtype), (None,))[0],
@@ -370,7 +557,8 @@ def run_b200(args):
                                                        (None, None))[1],
                      "kernel": ("paged_decode_stream_kernel" if st["partition_tokens"] < 0
                                 else "paged_decode_mma_kernel") + " + splitk_reduce_kernel",
-                     "launch_ms": round(dec_ms, 5), "peak_kind": peak_kind},
+                     "launch_ms": round(dec_ms, 5), "launch_spread": _spread(dec_reps),
+                     "peak_kind": peak_kind},
         "clocks": clk,
         "gpu_launches": launches_per_step * args.steps,
         "e2e": e2e,
@@ -480,9 +668,19 @@ def main():
                     help="KV cache dtype: the configuration's, or fp8 (e4m3) on the same workload")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="N>1 output all-gather: fused NVLink peer stores or NCCL")
+    ap.add_argument("--partition-tokens", type=int, default=None,
+                    help="split-K partition length (default: the library's choice; -1 balanced)")
+    ap.add_argument("--replays", type=int, default=30,
+                    help="individually timed graph replays behind spread and the roofline time")
+    ap.add_argument("--profile-share", type=int, default=0,
+                    help="ncu case: one rank's share of a W-way shard on one GPU (no JSON)")
+    ap.add_argument("--profile-rank", type=int, default=0)
+    ap.add_argument("--launches", type=int, default=6)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.impl == "reference":
+    if args.profile_share:
+        run_profile_share(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)

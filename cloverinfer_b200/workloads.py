@@ -166,5 +166,5 @@ def build_decode_step(cfg, rank, world, lens, device, seed=0, gather=None, n_new
 
     return dict(pool=pool, q=q, out=out, step=step, decode_only=decode_only, hkv_local=hkv_l,
                 hq_local=hq_l, kv_range=(lo, hi), partition_tokens=pt, workspace_bytes=nbytes,
-                rows=T, max_q=max_q)
+                rows=T, max_q=max_q, k_new=kn, v_new=vn, n_new=n_new, ctx_rows=ctx)
 
