@@ -50,6 +50,8 @@ SIGNATURES = {
     "clover_b200_block_free": (ctypes.c_int, [_P, _P, _I32, _P, _I32, _P, _P, _I32, _P, _P]),
     "clover_b200_compute_slots": (ctypes.c_int, [_P, _I32, _P, _P, _P, _I32, _I32, _I64, _P, _P, _P]),
     "clover_b200_kv_append": (ctypes.c_int, [_P, _P, _P, _P, _I64, _P, _I64, _I32, _I32, _I32, _I64, _I32, _P, _P]),
+    "clover_b200_kv_append_layers": (ctypes.c_int, [_P, _P, _I64, _P, _P, _I64, _I64, _P, _I64, _I32,
+                                                    _I32, _I32, _I32, _I64, _I32, _P, _P]),
     "clover_b200_decode_workspace_bytes": (ctypes.c_int64, [_I32] * 11),
     "clover_b200_decode_partition_tokens": (ctypes.c_int, [_I32] * 11),
     "clover_b200_paged_decode": (ctypes.c_int, [
@@ -186,6 +188,26 @@ def kv_append(k_cache, v_cache, k_new, v_new, slot_mapping, status):
         _ptr(slot_mapping), k_new.shape[0], h, d, bs, nb, dtype_code(k_cache.dtype),
         _ptr(status), _stream(k_cache.device))
     _check(rc, "clover_b200_kv_append")
+
+
+def kv_append_layers(k_layers, v_layers, k_new, v_new, slot_mapping, status):
+    """Every layer at once: caches [L, num_blocks, bs, H, D]; k_new/v_new
+    [L, n, H, D] views (layer and token strides free, each token's [H, D]
+    contiguous), one launch."""
+    _require_cuda(k_layers, v_layers, k_new, v_new, slot_mapping, status)
+    L, nb, bs, h, d = k_layers.shape
+    if k_new.dim() != 4 or k_new.shape[0] != L or k_new.shape[2:] != (h, d) or v_new.shape != k_new.shape:
+        raise ValueError(f"kv_append_layers: new K/V {tuple(k_new.shape)} != [{L}, n, {h}, {d}]")
+    if k_new.dtype != k_layers.dtype or v_new.dtype != k_layers.dtype:
+        raise TypeError("kv_append_layers: new K/V dtype must match the cache dtype")
+    if (k_new.stride(3) != 1 or k_new.stride(2) != d or v_new.stride() != k_new.stride()
+            or not k_layers.is_contiguous() or not v_layers.is_contiguous()):
+        raise ValueError("kv_append_layers: token rows and caches must be contiguous")
+    rc = lib().clover_b200_kv_append_layers(
+        _ptr(k_layers), _ptr(v_layers), k_layers.stride(0), _ptr(k_new), _ptr(v_new), k_new.stride(0),
+        k_new.stride(1), _ptr(slot_mapping), k_new.shape[1], L, h, d, bs, nb,
+        dtype_code(k_layers.dtype), _ptr(status), _stream(k_layers.device))
+    _check(rc, "clover_b200_kv_append_layers")
 
 
 # ---------------------------------------------------------------- decode
@@ -331,23 +353,29 @@ def decode_gather_workspace_bytes(n_seqs, n_rows, max_queries_per_seq, max_ctx_l
 
 def decode_step_gather(q, k_cache, v_cache, k_new, v_new, block_tables, query_start_loc, ctx_lens,
                        gather, *, max_queries_per_seq, max_ctx_len, score_scale, seq_rows=None,
-                       partition_tokens=0, workspace=None, status=None):
+                       partition_tokens=0, workspace=None, status=None, out=None):
     """decode_step whose output, all-gathered over every rank of ``gather`` (a
-    PeerGather), lands in ``gather.out[:rows]`` ([rows, Hq_total, D])."""
+    PeerGather), lands in ``out`` ([rows, Hq_total, D] in q's dtype, any row
+    stride, each row's heads contiguous: e.g. a view of the consumer's
+    [rows, Hq_total * D] input), by default ``gather.out[:rows]``."""
+    out = gather.out if out is None else out
     _require_cuda(q, k_cache, v_cache, k_new, v_new, block_tables, query_start_loc, ctx_lens,
-                  seq_rows, workspace, status)
+                  seq_rows, workspace, status, out)
     nb, bs, hkv, d = k_cache.shape
     rows, hq, dq = q.shape
     if dq != d or q.stride(2) != 1 or q.stride(1) != d:
         raise ValueError("decode_step_gather: q must be [rows, Hq_local, D] with contiguous rows")
-    if q.dtype != gather.out.dtype or rows > gather.out.shape[0] or hq * gather.world != gather.out.shape[1]:
-        raise ValueError("decode_step_gather: q does not fit the gather buffers")
+    if (q.dtype != out.dtype or rows > out.shape[0] or hq * gather.world != out.shape[1]
+            or out.dim() != 3 or out.shape[2] != d or out.stride(2) != 1 or out.stride(1) != d):
+        raise ValueError("decode_step_gather: out must be [>= rows, Hq_local * world, D] in q's dtype "
+                         "with each row's heads contiguous")
+    if rows * hq * gather.world * d > gather.half_words:
+        raise ValueError("decode_step_gather: more rows than the gather buffers hold")
     if k_new is not None and (k_new.shape != (rows, hkv, d) or v_new.shape != k_new.shape
                               or k_new.dtype != k_cache.dtype):
         raise ValueError("decode_step_gather: new K/V must be [rows, Hkv_local, D] in the cache dtype")
     n_seqs = query_start_loc.numel() - 1
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
-    out = gather.out
     rc = lib().clover_b200_decode_step_gather(
         _ptr(out), out.stride(0), _ptr(q), q.stride(0), dtype_code(q.dtype), _ptr(k_cache),
         _ptr(v_cache), dtype_code(k_cache.dtype), nb, bs, _ptr(k_new), _ptr(v_new),

@@ -47,6 +47,10 @@ from . import _lib
 from .kv_cache import PagedKVPool, auto_partition, to_device_i32
 
 
+_HOST_Q_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
+_ONE = (1,)  # n_new of a single-token batch, as _split reads it (its max)
+
+
 @dataclass
 class _Request:
     row: int
@@ -84,17 +88,25 @@ class _FastPlan:
         self.k = self.dev[self.k_off:self.v_off].view(k_dtype).view(B, *k_shape)
         self.v = self.dev[self.v_off:self.m_off].view(k_dtype).view(B, *k_shape)
         meta = self.dev[self.m_off:].view(torch.int32)
-        self.rows, self.offs, self.ctx = meta[0:B], meta[B:2 * B + 1], meta[2 * B + 1:]
+        self.rows, self.offs_d, self.ctx = meta[0:B], meta[B:2 * B + 1], meta[2 * B + 1:]
         self.meta = (ctypes.c_int32 * n_meta)()
         self.srcs = (ctypes.c_void_p * self.n)()
         self.sizes = (ctypes.c_int64 * self.n)(*([self.qb] * B + [self.kb] * (2 * B) + [4 * n_meta]))
         self.srcs[self.n - 1] = ctypes.addressof(self.meta)
+        self.offs_list = list(range(B + 1))  # one new token per item
         self.out = torch.empty((B, hq_total, q_shape[-1]), dtype=out_dtype, pin_memory=True)
         self.warm = False  # one eager call ran with this shape (one-time set-up done)
         self.graphs: Dict[tuple, "_StepGraph"] = {}
-        # device output and split-K workspace (per context bucket) shared by
-        # this shape's graphs: they replay one after another on one stream
-        self.out_dev: Optional[torch.Tensor] = None
+        # The captured steps' result buffer, shared by this shape's graphs (they
+        # replay one after another on one stream): the output [B, Hq, D] and,
+        # after it, the status word those steps' kernels raise bits in, so one
+        # D2H copy brings both back.
+        self.out_bytes = B * hq_total * q_shape[-1] * esz(out_dtype)
+        self.res_dev = torch.zeros(self.out_bytes + 16, dtype=torch.uint8, device=device)
+        self.out_dev = self.res_dev[:self.out_bytes].view(out_dtype).view(B, hq_total, q_shape[-1])
+        self.status_dev = self.res_dev[self.out_bytes:self.out_bytes + 4].view(torch.int32)
+        self.res_shape = (B, 1, hq_total, q_shape[-1])
+        self.out_dtype = out_dtype
         self.ws: Dict[tuple, Optional[torch.Tensor]] = {}  # by (bucket, split)
 
 
@@ -164,6 +176,10 @@ class B200AttentionBackend:
         self._fast: "OrderedDict[tuple, _FastPlan]" = OrderedDict()
         self.max_fast_plans = int(max_fast_plans)
         self.cuda_graphs = bool(cuda_graphs)
+        # prefill ingestion runs on a side stream; the decode stream waits for
+        # these events before it next reads or frees blocks
+        self._ingest_stream: Optional[torch.cuda.Stream] = None
+        self._pending_ingest: List[torch.cuda.Event] = []
 
     # ------------------------------------------------------------ setup
     def _ensure_pool(self, num_layers: int, heads: int, head_dim: int, dtype: torch.dtype) -> None:
@@ -199,9 +215,9 @@ class B200AttentionBackend:
         if self.shuffle_seed is not None:
             self.pool.shuffle_free_stack(self.shuffle_seed)
 
-    def _local_kv(self, x: torch.Tensor) -> torch.Tensor:
-        """[T, H, D] on device in the cache dtype, local KV heads only.  H may be
-        Hkv (native) or Hq = Hkv * g (repeat_kv-expanded: one head per group kept)."""
+    def _select_heads(self, x: torch.Tensor) -> torch.Tensor:
+        """View of [T, H, D] with this rank's KV heads only.  H may be Hkv
+        (native) or Hq = Hkv * g (repeat_kv-expanded: one head per group kept)."""
         h = x.shape[1]
         if h != self.num_kv_heads:
             if h % self.num_kv_heads:
@@ -210,7 +226,56 @@ class B200AttentionBackend:
         lo, hi = self.kv_range
         if (lo, hi) != (0, self.num_kv_heads):
             x = x[:, lo:hi]
-        return x.to(device=self.device, dtype=self.kv_dtype, non_blocking=True).contiguous()
+        return x
+
+    def _local_kv(self, x: torch.Tensor) -> torch.Tensor:
+        """[T, H, D] on device in the cache dtype, local KV heads only."""
+        return self._select_heads(x).to(device=self.device, dtype=self.kv_dtype,
+                                        non_blocking=True).contiguous()
+
+    def _ingest(self, row: int, initial_kv, T: int) -> None:
+        """Every layer's prefill K/V into the pool in one pass: this rank's
+        heads of all layers are gathered into one staging buffer [L, K|V, T,
+        Hkv_local, D] (pinned host memory for host inputs, so the H2D is one
+        asynchronous copy), then one slot computation and one multi-layer
+        append.  All of it runs on a side stream, overlapping whatever the
+        decode stream is doing; the decode stream waits for it before it next
+        reads or frees blocks (_await_ingest)."""
+        pool = self.pool
+        L = len(initial_kv)
+        hl = self.kv_range[1] - self.kv_range[0]
+        cur = torch.cuda.current_stream(self.device)
+        if self._ingest_stream is None:
+            self._ingest_stream = torch.cuda.Stream(self.device)
+        ing = self._ingest_stream
+        ing.wait_stream(cur)  # the blocks were reserved (and inputs made) on the decode stream
+        on_host = not initial_kv[0]["key"].is_cuda
+        with torch.cuda.stream(ing):
+            shape = (L, 2, T, hl, self.head_dim)
+            if on_host:
+                stage = torch.empty(shape, dtype=self.kv_dtype, pin_memory=True)
+            else:
+                stage = torch.empty(shape, dtype=self.kv_dtype, device=self.device)
+            for li, layer in enumerate(initial_kv):
+                for j, name in ((0, "key"), (1, "value")):
+                    src = layer[name]
+                    if src.is_cuda:
+                        src.record_stream(ing)  # read on this stream after the call returns
+                    stage[li, j].copy_(self._select_heads(src))
+            dev = stage.to(self.device, non_blocking=True) if on_host else stage
+            meta = to_device_i32([row, 0, 0, T], self.device)
+            slots = pool.slots(meta[0:1], meta[1:2], meta[2:4], T)
+            _lib.kv_append_layers(pool.k, pool.v, dev[:, 0], dev[:, 1], slots, pool.status)
+            ev = torch.cuda.Event()
+            ev.record(ing)
+        self._pending_ingest.append(ev)
+
+    def _await_ingest(self) -> None:
+        """Order the decode stream after every prefill ingestion issued so far."""
+        cur = torch.cuda.current_stream(self.device)
+        for ev in self._pending_ingest:
+            cur.wait_event(ev)
+        self._pending_ingest.clear()
 
     # ------------------------------------------------------------ interface
     def init_request(self, request_id: str, initial_kv: List[Dict[str, torch.Tensor]],
@@ -235,11 +300,7 @@ class B200AttentionBackend:
             pool._free_rows.append(row)
             raise
         if T > 0:
-            dev = self.device
-            meta = to_device_i32([row, 0, 0, T], dev)
-            slots = pool.slots(meta[0:1], meta[1:2], meta[2:4], T)
-            for li, layer in enumerate(initial_kv):
-                pool.append(li, self._local_kv(layer["key"]), self._local_kv(layer["value"]), slots)
+            self._ingest(row, initial_kv, T)
         self._reqs[request_id] = _Request(row=row, layer_len=[T] * self.num_layers, ctx=T)
         return T
 
@@ -249,6 +310,8 @@ class B200AttentionBackend:
     def free_request(self, request_id: str) -> None:
         req = self._reqs.pop(request_id, None)
         if req is not None:
+            if self._pending_ingest:
+                self._await_ingest()  # its blocks may still be being written
             self.pool.release_row(req.row)
 
     def decode_layer(self, request_id: str, layer_idx: int, query: torch.Tensor,
@@ -278,82 +341,121 @@ class B200AttentionBackend:
         return results  # type: ignore[return-value]
 
     def _run_items(self, items, layer: int, scale: float, results, base: int) -> None:
-        rids = [str(it["request_id"]) for it in items]
-        for r in rids:
-            if r not in self._reqs:
-                raise KeyError(f"Unknown request {r}")
-        sq = lambda t: t.squeeze(0) if t.dim() == 3 else t  # noqa: E731
-        qs = [sq(it["query"]) for it in items]
-        ks = [sq(it["key"]) for it in items]
-        vs = [sq(it["value"]) for it in items]
-        q_dtype, q_shape = qs[0].dtype, qs[0].shape
-        k_dtype, k_shape = ks[0].dtype, ks[0].shape
-        # the fast path gathers fixed byte counts per item: every item must have
-        # the first one's shapes and dtypes, on the host
-        uniform = q_dtype in (torch.float32, torch.float16, torch.bfloat16)
-        if uniform:
-            for t, kt, vt in zip(qs, ks, vs):
-                if (t.is_cuda or kt.is_cuda or vt.is_cuda or t.dtype != q_dtype
-                        or kt.dtype != k_dtype or vt.dtype != k_dtype or t.shape != q_shape
-                        or kt.shape != k_shape or vt.shape != k_shape):
-                    uniform = False
+        reqs_d = self._reqs
+        try:
+            reqs = [reqs_d[it["request_id"]] for it in items]
+        except (KeyError, TypeError):
+            reqs = []
+            for it in items:
+                rid = str(it["request_id"])
+                if rid not in reqs_d:
+                    raise KeyError(f"Unknown request {rid}") from None
+                reqs.append(reqs_d[rid])
+        qs = [it["query"] for it in items]
+        ks = [it["key"] for it in items]
+        vs = [it["value"] for it in items]
+        if qs[0].dim() == 3 or ks[0].dim() == 3 or vs[0].dim() == 3:
+            sq = lambda t: t.squeeze(0) if t.dim() == 3 else t  # noqa: E731
+            qs, ks, vs = [sq(t) for t in qs], [sq(t) for t in ks], [sq(t) for t in vs]
+        B = len(items)
+        q0, k0 = qs[0], ks[0]
+        key = (B, q0.shape, q0.dtype, k0.shape, k0.dtype)
+        plan = self._fast.get(key)
+        # The fast path gathers fixed byte counts per item into one pinned
+        # buffer: every item must be on the host with the first one's shapes
+        # and dtypes.
+        fast = plan is not None or (not q0.is_cuda and q0.dtype in _HOST_Q_DTYPES)
+        if fast:
+            if plan is None:
+                plan = _FastPlan(self.device, B, q0.shape, q0.dtype, k0.shape, k0.dtype, 3 * B + 1,
+                                 q0.dtype, q0.shape[0])
+                self._fast[key] = plan
+                while len(self._fast) > max(1, self.max_fast_plans):
+                    # every call ends with a stream sync: no evicted graph is in flight
+                    self._fast.popitem(last=False)
+            elif len(self._fast) > 1:
+                self._fast.move_to_end(key)
+            _, qsh, qdt, ksh, kdt = key
+            srcs = plan.srcs
+            for i in range(B):
+                t, kt, vt = qs[i], ks[i], vs[i]
+                if (t.shape != qsh or kt.shape != ksh or vt.shape != ksh or t.dtype != qdt
+                        or kt.dtype != kdt or vt.dtype != kdt or t.is_cuda or kt.is_cuda or vt.is_cuda):
+                    fast = False
                     break
-        if not uniform:  # device tensors (or mixed inputs): no staging, no host sync
+                if not (t.is_contiguous() and kt.is_contiguous() and vt.is_contiguous()):
+                    t, kt, vt = t.contiguous(), kt.contiguous(), vt.contiguous()
+                    qs[i], ks[i], vs[i] = t, kt, vt  # keep alive until the gather
+                srcs[i] = t.data_ptr()
+                srcs[B + i] = kt.data_ptr()
+                srcs[2 * B + i] = vt.data_ptr()
+        if not fast:  # device tensors (or mixed inputs): no staging, no host sync
+            rids = [str(it["request_id"]) for it in items]
             out = self.decode_batch(rids, layer, torch.stack(qs), torch.stack(ks), torch.stack(vs), scale)
             if not qs[0].is_cuda:
                 out = out.to("cpu")
-            if out.dtype != q_dtype:
-                out = out.to(q_dtype)
+            if out.dtype != q0.dtype:
+                out = out.to(q0.dtype)
             if self.check_status and not qs[0].is_cuda:
                 self.pool.check_status()
             for n in range(len(items)):
                 results[base + n] = out[n:n + 1]
             return
-        B = len(items)
-        n_new = [1] * B
-        reqs, rows, targets, offs, ctx_rows = self._plan(rids, layer, n_new, qs[0].shape)
-        q0, k0 = qs[0], ks[0]
-        key = (B, tuple(q0.shape), q_dtype, tuple(k0.shape), k0.dtype)
-        plan = self._fast.get(key)
-        if plan is None:
-            plan = _FastPlan(self.device, B, q0.shape, q_dtype, k0.shape, k0.dtype, 3 * B + 1,
-                             q_dtype, q0.shape[0])
-            self._fast[key] = plan
-            while len(self._fast) > max(1, self.max_fast_plans):
-                # every call ends with a stream sync, so no evicted graph is in flight
-                self._fast.popitem(last=False)
-        else:
-            self._fast.move_to_end(key)
-        # one native gather into the pinned staging buffer -> one H2D copy
-        srcs = plan.srcs
-        for i in range(B):
-            t, kt, vt = qs[i], ks[i], vs[i]
-            if not (t.is_contiguous() and kt.is_contiguous() and vt.is_contiguous()):
-                t, kt, vt = t.contiguous(), kt.contiguous(), vt.contiguous()
-                qs[i], ks[i], vs[i] = t, kt, vt  # keep alive until the gather
-            srcs[i] = t.data_ptr()
-            srcs[B + i] = kt.data_ptr()
-            srcs[2 * B + i] = vt.data_ptr()
-        plan.meta[:] = rows + offs + ctx_rows
+        if self._pending_ingest:
+            self._await_ingest()
+        rows, targets = self._plan_single(reqs, layer, q0.shape)
+        plan.meta[:] = rows + plan.offs_list + targets
         _lib.host_gather(srcs, plan.sizes, plan.n, plan.host.data_ptr())
-        pt = self._split(targets, n_new)
+        pt = self._split(targets, _ONE)
         step = self._step_graph(plan, layer, scale, max(targets), pt) if plan.warm else None
         if step is not None:
-            # one graph launch: H2D, fused step, D2H of output and status
+            # One graph launch (H2D, fused step); the copy of the output and
+            # status word into fresh pinned memory and the host bookkeeping
+            # run while the GPU works.
             step.graph.replay()
-            self._advance(reqs, layer, n_new, targets)
-        else:
-            plan.dev.copy_(plan.host, non_blocking=True)
-            out = self._launch(reqs, layer, n_new, targets, plan.q, plan.k, plan.v, plan.rows,
-                               plan.offs, plan.ctx, scale, check=False, pt=pt)
-            # output and status word back behind one synchronisation
-            plan.out.copy_(out, non_blocking=True)
-            self._status_host.copy_(self.pool.status, non_blocking=True)
-            plan.warm = True
+            res = plan.res_dev.to("cpu", non_blocking=True)
+            outs = res[:plan.out_bytes].view(plan.out_dtype).view(plan.res_shape).unbind(0)
+            status = res[plan.out_bytes:plan.out_bytes + 4].view(torch.int32)
+            self._advance(reqs, layer, None, targets)
+            torch.cuda.current_stream(self.device).synchronize()
+            code = int(status[0])
+            if code:
+                plan.status_dev.zero_()
+                if self.check_status:
+                    self.pool.raise_status(code)
+            results[base:base + B] = outs
+            return
+        plan.dev.copy_(plan.host, non_blocking=True)
+        out = self._launch(reqs, layer, [1] * B, targets, plan.q, plan.k, plan.v, plan.rows,
+                           plan.offs_d, plan.ctx, scale, check=False, pt=pt)
+        # output and status word back behind one synchronisation
+        plan.out.copy_(out, non_blocking=True)
+        self._status_host.copy_(self.pool.status, non_blocking=True)
+        plan.warm = True
         torch.cuda.current_stream(self.device).synchronize()
         if self.check_status and int(self._status_host[0]):
             self.pool.check_status()
         results[base:base + B] = plan.out.clone().split(1)
+
+    def _plan_single(self, reqs, layer: int, q_shape):
+        """_plan for one new token per request: validate, reserve the blocks
+        the new tokens need; returns (table rows, contexts after the step)."""
+        pool = self.pool
+        if not 0 <= layer < self.num_layers:
+            raise IndexError(f"layer_idx {layer} out of range [0, {self.num_layers})")
+        hq, d = int(q_shape[0]), int(q_shape[1])
+        if hq % self.num_kv_heads or d != self.head_dim:
+            raise ValueError(f"query heads x dim {hq} x {d} do not fit {self.num_kv_heads} KV heads x {self.head_dim}")
+        rows = [r.row for r in reqs]
+        targets = [r.layer_len[layer] + 1 for r in reqs]
+        cap = pool.block_size
+        blocks = pool.row_blocks
+        # (rows are distinct: decode_layer_batch never puts one request twice in a group)
+        for r, t in zip(rows, targets):
+            if t > blocks[r] * cap:  # some row crosses into a new block
+                pool.reserve(rows, targets, "OOM during append")
+                break
+        return rows, targets
 
     # Context lengths are rounded up to this many tokens for a captured step:
     # the launch's max_ctx_len (and so its partition plan and workspace) is
@@ -417,29 +519,26 @@ class B200AttentionBackend:
             plan.ws[key[2:]] = (torch.empty(nbytes, dtype=torch.uint8, device=self.device)
                                 if nbytes > 0 else None)
         ws = plan.ws[key[2:]]
-        if peer is None and plan.out_dev is None:
-            plan.out_dev = torch.empty_like(q)
-        out_dev = None if peer is not None else plan.out_dev
+        out_dev = plan.out_dev
         g = torch.cuda.CUDAGraph()
         try:
             with torch.cuda.graph(g):
+                # H2D of the staging buffer, then the fused step writing the
+                # (all-gathered) output and its status bits into the plan's
+                # result buffer; the caller copies that back after the launch.
                 plan.dev.copy_(plan.host, non_blocking=True)
                 if peer is not None:
                     _lib.decode_step_gather(q, pool.k[layer], pool.v[layer], k_loc, v_loc, pool.tables,
-                                            plan.offs, plan.ctx, peer, max_queries_per_seq=1,
+                                            plan.offs_d, plan.ctx, peer, max_queries_per_seq=1,
                                             max_ctx_len=bucket, score_scale=scale, seq_rows=plan.rows,
                                             partition_tokens=pt, workspace=ws,
-                                            status=pool.status)
-                    src = peer.out[:B]
+                                            status=plan.status_dev, out=out_dev)
                 else:
                     _lib.decode_step(out_dev, q, pool.k[layer], pool.v[layer], k_loc, v_loc, pool.tables,
-                                     plan.offs, plan.ctx, max_queries_per_seq=1, max_ctx_len=bucket,
+                                     plan.offs_d, plan.ctx, max_queries_per_seq=1, max_ctx_len=bucket,
                                      score_scale=scale, seq_rows=plan.rows,
                                      partition_tokens=pt, workspace=ws,
-                                     status=pool.status, check=False)
-                    src = out_dev
-                plan.out.copy_(src, non_blocking=True)
-                self._status_host.copy_(pool.status, non_blocking=True)
+                                     status=plan.status_dev, check=False)
         except Exception as e:  # capture is not available here: stay eager from now on
             warnings.warn(f"B200AttentionBackend: CUDA graph capture failed ({e!r}); "
                           "using eager launches", RuntimeWarning)
@@ -464,6 +563,8 @@ class B200AttentionBackend:
         T = sum(n_new)
         if query.shape[0] != T or key.shape[0] != T or value.shape[0] != T:
             raise ValueError(f"expected {T} new tokens, got q {tuple(query.shape)} k {tuple(key.shape)}")
+        if self._pending_ingest:
+            self._await_ingest()
         reqs, rows, targets, offs, ctx_rows = self._plan(request_ids, layer_idx, n_new, query.shape[1:])
         meta = to_device_i32(rows + offs + ctx_rows, self.device)
         out = self._launch(reqs, layer_idx, n_new, targets, query, key, value, meta[0:B],
@@ -533,16 +634,23 @@ class B200AttentionBackend:
 
     def _advance(self, reqs, layer_idx, n_new, targets) -> None:
         """Host bookkeeping of a launched step: per-layer lengths, context
-        (after the last layer) and counters."""
+        (after the last layer) and counters.  n_new None: one token each."""
         lo, hi = self.kv_range
-        for r, n in zip(reqs, n_new):
-            r.layer_len[layer_idx] += n
-            if layer_idx == self.num_layers - 1:
-                r.ctx += n
+        last = layer_idx == self.num_layers - 1
+        if n_new is None:
+            for r in reqs:
+                r.layer_len[layer_idx] += 1
+                if last:
+                    r.ctx += 1
+        else:
+            for r, n in zip(reqs, n_new):
+                r.layer_len[layer_idx] += n
+                if last:
+                    r.ctx += n
         st = self.stats
         st.batches += 1
         st.items += len(reqs)
-        st.tokens += sum(n_new)
+        st.tokens += len(reqs) if n_new is None else sum(n_new)
         st.kv_bytes_read += sum(targets) * (hi - lo) * self.head_dim * 2 * self._kv_esz
 
     def _peer_for(self, q: torch.Tensor):

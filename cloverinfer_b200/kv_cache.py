@@ -227,11 +227,16 @@ class PagedKVPool:
         code = int(self.status.item())
         if code:
             self.status.zero_()
-            names = [n for n, bit in [("bad slot", _lib.DEV_BAD_SLOT), ("bad block id", _lib.DEV_BAD_BLOCK),
-                                      ("table full", _lib.DEV_TABLE_FULL), ("out of blocks", _lib.DEV_OOM),
-                                      ("wait timeout", _lib.DEV_TIMEOUT), ("context > max_ctx_len", _lib.DEV_CTX_RANGE)]
-                     if code & bit]
-            raise RuntimeError(f"libclover_b200 device status 0x{code:x}: {', '.join(names)}")
+            self.raise_status(code)
+
+    @staticmethod
+    def raise_status(code: int) -> None:
+        """Raise the RuntimeError that names the CLOVER_B200_DEV_* bits of ``code``."""
+        names = [n for n, bit in [("bad slot", _lib.DEV_BAD_SLOT), ("bad block id", _lib.DEV_BAD_BLOCK),
+                                  ("table full", _lib.DEV_TABLE_FULL), ("out of blocks", _lib.DEV_OOM),
+                                  ("wait timeout", _lib.DEV_TIMEOUT), ("context > max_ctx_len", _lib.DEV_CTX_RANGE)]
+                 if code & bit]
+        raise RuntimeError(f"libclover_b200 device status 0x{code:x}: {', '.join(names)}")
 
     def row_table(self, row: int) -> List[int]:
         n = self.row_blocks[row]

@@ -162,6 +162,26 @@ CLOVER_B200_API int clover_b200_kv_append(void* k_cache, void* v_cache, const vo
                           int64_t num_blocks, int32_t dtype, int32_t* dev_status, void* stream);
 
 /*
+ * KV append for n_layers layers in one launch: layer l's new tokens start at
+ * k_new / v_new + l * new_layer_stride elements (token stride
+ * new_token_stride, as in clover_b200_kv_append) and go to the caches at
+ * k_cache / v_cache + l * cache_layer_stride elements, every layer through
+ * the same slot_mapping (all layers of a sequence hold the same tokens).
+ * Used to ingest a request's prefill KV of every layer from one staging
+ * buffer.  Layer regions must not overlap (the strides are checked).
+ * Replaces: the per-layer initial_kv load of CpuAttentionBackend.init_request
+ * (attention_backend.py:68-80) fed by the prefill KV export
+ * (model_adapter.py:173-182), and KVCacheManager.load_initial_kv
+ * (memory_manager.py:74-93) repeated per layer.
+ */
+CLOVER_B200_API int clover_b200_kv_append_layers(void* k_cache, void* v_cache, int64_t cache_layer_stride,
+                          const void* k_new, const void* v_new, int64_t new_layer_stride,
+                          int64_t new_token_stride, const int64_t* slot_mapping, int64_t n_tokens,
+                          int32_t n_layers, int32_t num_kv_heads, int32_t head_dim,
+                          int32_t block_size, int64_t num_blocks, int32_t dtype,
+                          int32_t* dev_status, void* stream);
+
+/*
  * partition_tokens = CLOVER_B200_PARTITION_BALANCED asks for the balanced
  * split on the tensor-core path (bf16/fp16 cache, head_dim 64/128/256, block
  * 16/32, at most 1024 sequences): the KV blocks of all sequences are divided

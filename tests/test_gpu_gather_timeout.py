@@ -114,7 +114,7 @@ def test_gather_wait_times_out_and_the_next_call_runs_clean():
     assert_attn_close(out[:, :hq_l], ref, kv_dtype=torch.bfloat16, what="own heads after timeout")
 
     # The pool's status check raises on the bit (and clears the word).
-    pool = SimpleNamespace(status=st)
+    pool = SimpleNamespace(status=st, raise_status=PagedKVPool.raise_status)
     with pytest.raises(RuntimeError, match="wait timeout"):
         PagedKVPool.check_status(pool)
     assert int(st.item()) == 0

@@ -134,3 +134,56 @@ def test_decode_step_matches_append_then_decode(dt, D, bs, n_new, hq, hkv):
         caches.append((pool.k.cpu(), pool.v.cpu()))
     assert torch.equal(caches[0][0], caches[1][0]) and torch.equal(caches[0][1], caches[1][1])
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("src", ["host", "device"])
+@pytest.mark.parametrize("expanded", [False, True])
+def test_prefill_ingestion_every_layer_bit_exact(src, expanded):
+    """init_request ingests every layer's prefill K/V (attention_backend.py:68-80)
+    through one staging buffer and one multi-layer append on a side stream: the
+    cache then holds, bit for bit, what KVCacheOracle.load_initial_kv
+    (memory_manager.py:74-93) stores for each layer, with the same block
+    tables; a decode issued right after it sees the ingested KV."""
+    from cloverinfer_b200 import B200AttentionBackend
+    from oracle import KVCacheOracle, repeat_kv
+    L, hkv, grp, D, bs, nb = 4, 2, 4, 128, 16, 64
+    dt = torch.bfloat16
+    be = B200AttentionBackend(device="cuda", num_blocks=nb, block_size=bs, num_kv_heads=hkv,
+                              kv_dtype=dt, max_seqs=4)
+    orc = [KVCacheOracle(nb, bs, hkv, D, dtype=dt) for _ in range(L)]
+    g = torch.Generator().manual_seed(21)
+    for rid, T in [("a", 37), ("b", 100), ("c", 16)]:
+        layers = [{"key": torch.randn(T, hkv, D, generator=g), "value": torch.randn(T, hkv, D, generator=g)}
+                  for _ in range(L)]  # fp32 inputs: the cache rounds them to bf16
+        feed = [{k: (repeat_kv(t, grp) if expanded else t) for k, t in l.items()} for l in layers]
+        if src == "device":
+            feed = [{k: t.cuda() for k, t in l.items()} for l in feed]
+        assert be.init_request(rid, feed) == T
+        for li in range(L):
+            orc[li].load_initial_kv(rid, layers[li]["key"], layers[li]["value"])
+        table = be.pool.row_table(be._reqs[rid].row)
+        assert table == orc[0].block_tables[rid]
+        slots = torch.tensor([table[t // bs] * bs + t % bs for t in range(T)])
+        for li in range(L):
+            kc = be.pool.k[li].reshape(-1, hkv, D)[slots.cuda()].cpu()
+            vc = be.pool.v[li].reshape(-1, hkv, D)[slots.cuda()].cpu()
+            ko = orc[li].k_cache.reshape(-1, hkv, D)[slots]
+            vo = orc[li].v_cache.reshape(-1, hkv, D)[slots]
+            assert torch.equal(kc.view(torch.int16), ko.view(torch.int16)), (rid, li)
+            assert torch.equal(vc.view(torch.int16), vo.view(torch.int16)), (rid, li)
+    be.pool.check_status()
+    # a decode issued right after the ingestion sees it (stream ordering)
+    q = torch.randn(hkv * grp, D, generator=g)
+    kn = torch.randn(hkv, D, generator=g).to(dt)
+    out = be.decode_layer("b", 0, q, kn, kn)
+    keys = torch.cat([orc[0].k_cache.reshape(-1, hkv, D)[torch.tensor(
+        [orc[0].block_tables["b"][t // bs] * bs + t % bs for t in range(100)])], kn[None]])
+    vals = torch.cat([orc[0].v_cache.reshape(-1, hkv, D)[torch.tensor(
+        [orc[0].block_tables["b"][t // bs] * bs + t % bs for t in range(100)])], kn[None]])
+    from oracle import attend
+    ref = attend(q, repeat_kv(keys, grp), repeat_kv(vals, grp), 1.0)
+    assert float((out[0] - ref).abs().max()) < 2e-3
+    for rid in ("a", "b", "c"):
+        be.free_request(rid)
+    assert be.pool.free_count == nb
+

@@ -105,3 +105,12 @@ def test_clover_kernels_shim_rejects_bad_shapes_on_cpu():
     with pytest.raises(ValueError):
         clover_kernels.paged_attention(torch.zeros_like(q), q, kc, kc, torch.zeros(2, 1, dtype=torch.int32),
                                        torch.ones(2, dtype=torch.int32), 8, 1)
+
+
+def test_append_layers_strides_checked():
+    """Overlapping layer strides are rejected before any launch (no GPU work)."""
+    lib = _lib.lib()
+    rc = lib.clover_b200_kv_append_layers(1 << 12, 1 << 13, 16, 1 << 14, 1 << 15, 8, 128, 1 << 16, 4, 2,
+                                          1, 128, 16, 8, _lib.BF16, None, None)
+    assert rc == _lib.ERR_INVALID_ARG
+    assert b"overlap" in lib.clover_b200_last_error()
