@@ -70,6 +70,10 @@ SIGNATURES = {
         _P, _I64, _P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _P, _I64, _P, _I32, _P, _P, _P,
         _I32, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _P, _I32, _I32, _I64, _P, _I64,
         _P, _P]),
+    "clover_b200_decode_step_gather_into": (ctypes.c_int, [
+        _P, _I64, _I32, _P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _P, _I64, _P, _I32, _P, _P, _P,
+        _I32, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _P, _I32, _I32, _I64, _P, _I64,
+        _P, _P]),
     "clover_b200_paged_decode_noalloc": (ctypes.c_int, [
         _P, _I64, _P, _I64, _I32, _P, _P, _I32, _I64, _I32, _P, _I32, _P, _P, _P,
         _I32, _I32, _I32, _I32, _I32, _I32, _I32, _F, _I32, _P, _P]),
@@ -355,9 +359,10 @@ def decode_step_gather(q, k_cache, v_cache, k_new, v_new, block_tables, query_st
                        gather, *, max_queries_per_seq, max_ctx_len, score_scale, seq_rows=None,
                        partition_tokens=0, workspace=None, status=None, out=None):
     """decode_step whose output, all-gathered over every rank of ``gather`` (a
-    PeerGather), lands in ``out`` ([rows, Hq_total, D] in q's dtype, any row
-    stride, each row's heads contiguous: e.g. a view of the consumer's
-    [rows, Hq_total * D] input), by default ``gather.out[:rows]``."""
+    PeerGather), lands in ``out`` ([rows, Hq_total, D] in f32/f16/bf16, any
+    row stride, each row's heads contiguous: e.g. a view of the consumer's
+    [rows, Hq_total * D] input in the model's dtype), by default
+    ``gather.out[:rows]``."""
     out = gather.out if out is None else out
     _require_cuda(q, k_cache, v_cache, k_new, v_new, block_tables, query_start_loc, ctx_lens,
                   seq_rows, workspace, status, out)
@@ -365,10 +370,11 @@ def decode_step_gather(q, k_cache, v_cache, k_new, v_new, block_tables, query_st
     rows, hq, dq = q.shape
     if dq != d or q.stride(2) != 1 or q.stride(1) != d:
         raise ValueError("decode_step_gather: q must be [rows, Hq_local, D] with contiguous rows")
-    if (q.dtype != out.dtype or rows > out.shape[0] or hq * gather.world != out.shape[1]
-            or out.dim() != 3 or out.shape[2] != d or out.stride(2) != 1 or out.stride(1) != d):
-        raise ValueError("decode_step_gather: out must be [>= rows, Hq_local * world, D] in q's dtype "
-                         "with each row's heads contiguous")
+    if (out.dtype not in (torch.float32, torch.float16, torch.bfloat16) or out.dim() != 3
+            or rows > out.shape[0] or hq * gather.world != out.shape[1] or out.shape[2] != d
+            or out.stride(2) != 1 or out.stride(1) != d):
+        raise ValueError("decode_step_gather: out must be [>= rows, Hq_local * world, D] "
+                         "(f32/f16/bf16) with each row's heads contiguous")
     if rows * hq * gather.world * d > gather.half_words:
         raise ValueError("decode_step_gather: more rows than the gather buffers hold")
     if k_new is not None and (k_new.shape != (rows, hkv, d) or v_new.shape != k_new.shape
@@ -376,6 +382,17 @@ def decode_step_gather(q, k_cache, v_cache, k_new, v_new, block_tables, query_st
         raise ValueError("decode_step_gather: new K/V must be [rows, Hkv_local, D] in the cache dtype")
     n_seqs = query_start_loc.numel() - 1
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    if out.dtype != q.dtype:
+        rc = lib().clover_b200_decode_step_gather_into(
+            _ptr(out), out.stride(0), dtype_code(out.dtype), _ptr(q), q.stride(0), dtype_code(q.dtype),
+            _ptr(k_cache), _ptr(v_cache), dtype_code(k_cache.dtype), nb, bs, _ptr(k_new), _ptr(v_new),
+            0 if k_new is None else k_new.stride(0), _ptr(block_tables), block_tables.stride(0),
+            _ptr(seq_rows), _ptr(query_start_loc), _ptr(ctx_lens), n_seqs, rows,
+            max_queries_per_seq, max_ctx_len, hq, hkv, d, float(score_scale), partition_tokens,
+            gather.peer_recv_d.data_ptr(), gather.sync.data_ptr(), gather.world, gather.rank,
+            gather.half_words, _ptr(workspace), ws_bytes, _ptr(status), _stream(q.device))
+        _check(rc, "clover_b200_decode_step_gather_into")
+        return
     rc = lib().clover_b200_decode_step_gather(
         _ptr(out), out.stride(0), _ptr(q), q.stride(0), dtype_code(q.dtype), _ptr(k_cache),
         _ptr(v_cache), dtype_code(k_cache.dtype), nb, bs, _ptr(k_new), _ptr(v_new),

@@ -144,6 +144,8 @@ class B200AttentionBackend:
         self.device = torch.device(device) if device is not None else _default_device()
         if self.device.type != "cuda":
             raise RuntimeError("B200AttentionBackend requires a CUDA device (no CPU fallback)")
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         _lib.lib()  # fail loudly if the CUDA library cannot be built or loaded
         self.block_size = int(block_size)
         self.max_seqs = int(max_seqs)
@@ -551,12 +553,20 @@ class B200AttentionBackend:
     # ------------------------------------------------------------ tensor API
     def decode_batch(self, request_ids: Sequence[str], layer_idx: int, query: torch.Tensor,
                      key: torch.Tensor, value: torch.Tensor, score_scale: float = 1.0,
-                     n_new: Optional[Sequence[int]] = None) -> torch.Tensor:
+                     n_new: Optional[Sequence[int]] = None,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Append ``n_new[b]`` tokens per request and attend causally.
 
         query [T, Hq, D] (fp32, or the cache dtype), key/value [T, Hkv or Hq, D];
         returns [T, Hq, D] on the GPU in the query dtype (all heads: sharded
         backends all-gather).  Enqueued on the current stream; no host sync.
+
+        ``out``: the consumer's buffer to receive the output instead, e.g. the
+        dense node's o_proj input (model_adapter.py:572): a device tensor whose
+        T rows each hold Hq * D contiguous values ([T, Hq * D], [T, 1, Hq * D]
+        or [T, Hq, D], any row stride), f32/f16/bf16.  A sharded backend's fused
+        gather writes every rank's heads straight into it; returned as a
+        [T, Hq, D] view.
         """
         B = len(request_ids)
         n_new = [1] * B if n_new is None else [int(n) for n in n_new]
@@ -565,12 +575,32 @@ class B200AttentionBackend:
             raise ValueError(f"expected {T} new tokens, got q {tuple(query.shape)} k {tuple(key.shape)}")
         if self._pending_ingest:
             self._await_ingest()
+        dst = None if out is None else self._consumer_view(out, T, query.shape[1])
         reqs, rows, targets, offs, ctx_rows = self._plan(request_ids, layer_idx, n_new, query.shape[1:])
         meta = to_device_i32(rows + offs + ctx_rows, self.device)
-        out = self._launch(reqs, layer_idx, n_new, targets, query, key, value, meta[0:B],
-                           meta[B:2 * B + 1], meta[2 * B + 1:], score_scale)
+        res = self._launch(reqs, layer_idx, n_new, targets, query, key, value, meta[0:B],
+                           meta[B:2 * B + 1], meta[2 * B + 1:], score_scale, dst=dst)
+        if dst is not None:
+            if res.data_ptr() != dst.data_ptr():
+                dst.copy_(res)
+            return dst
         # the fused gather's buffer is rewritten by the next call
-        return out.clone() if self._peer is not None and out.data_ptr() == self._peer.out.data_ptr() else out
+        return res.clone() if self._peer is not None and res.data_ptr() == self._peer.out.data_ptr() else res
+
+    def _consumer_view(self, out: torch.Tensor, T: int, hq: int) -> torch.Tensor:
+        """[T, Hq, D] view of a consumer buffer whose T rows hold Hq * D values."""
+        D = self.head_dim
+        if not out.is_cuda or out.device != self.device:
+            raise ValueError(f"out must be on {self.device}")
+        if out.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+            raise TypeError(f"out dtype {out.dtype} is not f32/f16/bf16")
+        if out.dim() < 2 or out.shape[0] != T:
+            raise ValueError(f"out must have {T} rows, got {tuple(out.shape)}")
+        rows = out.flatten(1) if out.dim() > 2 else out
+        if (rows.shape[1] != hq * D or rows.stride(1) != 1
+                or (out.dim() > 2 and rows.data_ptr() != out.data_ptr())):
+            raise ValueError(f"each row of out must hold {hq} x {D} contiguous values")
+        return rows.as_strided((T, hq, D), (rows.stride(0), D, 1))
 
     def _plan(self, request_ids, layer_idx: int, n_new, q_shape):
         """Validate, reserve blocks for the new tokens and build the metadata
@@ -601,7 +631,7 @@ class B200AttentionBackend:
         return reqs, rows, targets, offs, ctx_rows
 
     def _launch(self, reqs, layer_idx, n_new, targets, query, key, value, rows_d, offs_d, ctx_d,
-                score_scale, check: bool = True, pt: Optional[int] = None):
+                score_scale, check: bool = True, pt: Optional[int] = None, dst=None):
         pool = self.pool
         if pt is None:
             pt = self._split(targets, n_new)
@@ -621,12 +651,13 @@ class B200AttentionBackend:
             # fused append + decode + reduce with the all-gather over NVLink
             out = pool.decode_step_gather(layer_idx, q, self._local_kv(key), self._local_kv(value),
                                           offs_d, ctx_d, rows_d, max(n_new), max(targets),
-                                          score_scale, peer, partition_tokens=pt)
+                                          score_scale, peer, partition_tokens=pt, out=dst)
         else:
             # one launch: append each row's token at ctx - 1, then attend (+ reduce)
+            direct = dst is not None and not sharded and dst.dtype == q.dtype
             out = pool.decode_step(layer_idx, q, self._local_kv(key), self._local_kv(value), offs_d,
                                    ctx_d, rows_d, max(n_new), max(targets), score_scale,
-                                   partition_tokens=pt, check=check)
+                                   out=dst if direct else None, partition_tokens=pt, check=check)
         self._advance(reqs, layer_idx, n_new, targets)
         if sharded and peer is None:
             out = self.shard.gather(out, self.num_kv_heads, group)

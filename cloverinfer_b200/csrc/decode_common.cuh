@@ -46,6 +46,7 @@ struct DecodeArgs {
   const void* q;
   int64_t q_stride;
   int32_t q_dtype;
+  int32_t out_dtype;  // the output's type (the query's, except for a gather into a consumer buffer)
   const void* k_cache;
   const void* v_cache;
   const int32_t* tables;
@@ -135,7 +136,7 @@ __device__ __forceinline__ float load_q(const DecodeArgs& a, int64_t idx) {
 }
 
 __device__ __forceinline__ void store_out(const DecodeArgs& a, int64_t idx, float v) {
-  switch (a.q_dtype) {
+  switch (a.out_dtype) {
     case CLOVER_B200_F32: static_cast<float*>(a.out)[idx] = v; break;
     case CLOVER_B200_F16: static_cast<__half*>(a.out)[idx] = __float2half_rn(v); break;
     default: static_cast<__nv_bfloat16*>(a.out)[idx] = __float2bfloat16_rn(v); break;

@@ -526,7 +526,6 @@ constexpr int kReduceDims = 32;
 // partitions), folding them into a running (max, sum, value); the four warps
 // are merged in shared memory.  Every thread of the CTA must call it; the
 // result is valid in warp 0.
-constexpr int kPartsPerWarp = 16;         // splitk_reduce_kernel (6 CTAs per SM)
 constexpr int kGatherPartsPerWarp = 32;   // reduce_gather_kernel (a small grid)
 
 // Partials of (query row r, head h): from the partition length for the
@@ -596,23 +595,132 @@ __device__ __forceinline__ float reduce_unit(const DecodeArgs& a, int r, int h, 
   return v;
 }
 
-__global__ void __launch_bounds__(kReduceWarps * 32, 6)
-splitk_reduce_kernel(const DecodeArgs a, int D) {
-  __shared__ float s_m[kReduceWarps], s_l[kReduceWarps];
-  __shared__ float s_o[kReduceWarps][kReduceDims];
+// Split-K reduce for paged_decode / decode_step.  A unit is one (query row,
+// head); a CTA of 4 warps first screens up to 128 of its units at once (one
+// round trip for their contexts or part counts) and then reduces only those
+// with several partials: the CTA's threads take the log-sum-exp values (max,
+// then the sum of the weights), then warp w adds partitions w, w + 4, ...
+// of every dim (lane l: dims l, l + 32, ...; 8 partitions' loads in flight),
+// and the four warp sums are added in shared memory.  Units the decode wrote
+// itself (one partition) cost only the screening load, so a ragged batch
+// whose rows mostly fit one partition launches no CTA per (row, head).
+constexpr int kRedThreads = kReduceWarps * 32;
+constexpr int kRedBatch = 8;  // partitions per warp in flight
+
+template <int EPL>
+__device__ __forceinline__ void reduce_rows_unit(const DecodeArgs& a, int r, int h, int npp,
+                                                 int D, float* s_red, float (*s_o)[32 * EPL]) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t base = ((int64_t)r * a.num_q_heads + h) * a.max_parts;
+  // (1) max and sum of the weights 2^(lse_p - M) over the partitions
+  float mx = -INFINITY;
+  for (int p = tid; p < npp; p += kRedThreads) mx = fmaxf(mx, __ldcg(a.part_lse + base + p));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if (lane == 0) s_red[warp] = mx;
+  __syncthreads();
+  const float M = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
+  const float u = M == -INFINITY ? 0.f : M;
+  float sum = 0.f;
+  for (int p = tid; p < npp; p += kRedThreads) sum += fast_exp2(__ldcg(a.part_lse + base + p) - u);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+  if (lane == 0) s_red[4 + warp] = sum;
+  // (2) weighted sum of the partial outputs
+  float acc[EPL];
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) acc[j] = 0.f;
+  for (int p0 = warp; p0 < npp; p0 += kReduceWarps * kRedBatch) {
+    float wv[kRedBatch], v[kRedBatch][EPL];
+#pragma unroll
+    for (int i = 0; i < kRedBatch; ++i) {
+      const int p = p0 + i * kReduceWarps;
+      const bool ok = p < npp;
+      wv[i] = ok ? __ldcg(a.part_lse + base + p) : -INFINITY;
+#pragma unroll
+      for (int j = 0; j < EPL; ++j) {
+        const int d = lane + 32 * j;
+        v[i][j] = (ok && d < D) ? __ldcg(a.part_out + (base + p) * D + d) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kRedBatch; ++i) {
+      const float wi = fast_exp2(wv[i] - u);
+#pragma unroll
+      for (int j = 0; j < EPL; ++j) acc[j] = fmaf(wi, v[i][j], acc[j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) s_o[warp][lane + 32 * j] = acc[j];
+  __syncthreads();
+  const float L = s_red[4] + s_red[5] + s_red[6] + s_red[7];
+  for (int d = tid; d < D; d += kRedThreads) {
+    const float o = s_o[0][d] + s_o[1][d] + s_o[2][d] + s_o[3][d];
+    store_out(a, (int64_t)r * a.out_stride + (int64_t)h * D + d, L > 0.f ? o / L : 0.f);
+  }
+  __syncthreads();  // shared scratch is reused by the next unit
+}
+
+template <int EPL>
+__global__ void __launch_bounds__(kRedThreads)
+splitk_reduce_kernel(const DecodeArgs a, int D, int n_units) {
+  __shared__ float s_red[8];
+  __shared__ float s_o[kReduceWarps][32 * EPL];
+  __shared__ int s_unit[kRedThreads], s_npp[kRedThreads];
+  __shared__ int s_n;
   pdl_wait();     // every partial of the decode kernel is written
   pdl_trigger();  // the next step's kernel may start launching (it waits too)
-  const int r = blockIdx.x;
-  const int h = blockIdx.y;
-  const int lim = __ldg(a.ctx + r);
-  const int npp = partial_count(a, r, h, lim);
-  // Single-partition rows were written by the decode kernel, and so were the
-  // empty rows of the partition kernels; the stream kernel leaves those here.
-  if (npp == 1 || (npp == 0 && a.part_count == nullptr)) return;
-  const int lane = threadIdx.x & 31;
-  const int dim = blockIdx.z * kReduceDims + lane;
-  const float v = reduce_unit<kPartsPerWarp>(a, r, h, dim, D, npp, s_m, s_l, s_o);
-  if (threadIdx.x < 32 && dim < D) store_out(a, (int64_t)r * a.out_stride + (int64_t)h * D + dim, v);
+  const int tid = threadIdx.x;
+  const int H = a.num_q_heads;
+  for (int64_t round = 0;; ++round) {
+    const int64_t first = (int64_t)blockIdx.x + round * kRedThreads * gridDim.x;
+    if (first >= n_units) break;
+    if (tid == 0) s_n = 0;
+    __syncthreads();
+    const int64_t uu = first + (int64_t)tid * gridDim.x;
+    if (uu < n_units) {
+      const int u = (int)uu;
+      const int r = u / H, h = u - r * H;
+      const int npp = partial_count(a, r, h, __ldg(a.ctx + r));
+      // Single-partition rows were written by the decode kernel, and so were
+      // the empty rows of the partition kernels; the stream kernel leaves
+      // those here.
+      if (npp > 1 || (npp == 0 && a.part_count != nullptr)) {
+        const int i = atomicAdd(&s_n, 1);
+        s_unit[i] = u;
+        s_npp[i] = npp;
+      }
+    }
+    __syncthreads();
+    const int n = s_n;
+    for (int i = 0; i < n; ++i) {
+      const int u = s_unit[i];
+      const int r = u / H, h = u - r * H;
+      reduce_rows_unit<EPL>(a, r, h, s_npp[i], D, s_red, s_o);
+    }
+    __syncthreads();  // everyone read s_n before the next round resets it
+  }
+}
+
+static int launch_splitk_reduce(const DecodeArgs& a, int D, int n_rows, cudaStream_t s) {
+  const int64_t units = (int64_t)n_rows * a.num_q_heads;
+  if (units <= 0) return CLOVER_B200_OK;
+  if (units > INT32_MAX) return set_error(CLOVER_B200_ERR_UNSUPPORTED, "splitk_reduce: too many rows");
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t cap = (int64_t)sms * 16;
+  const dim3 grid((unsigned)(units < cap ? units : cap));
+  const int epl = (D + 31) / 32;
+  cudaError_t e;
+  switch (epl) {
+    case 1: e = launch_pdl(splitk_reduce_kernel<1>, grid, dim3(kRedThreads), 0, s, a, D, (int)units); break;
+    case 2: e = launch_pdl(splitk_reduce_kernel<2>, grid, dim3(kRedThreads), 0, s, a, D, (int)units); break;
+    case 3: e = launch_pdl(splitk_reduce_kernel<3>, grid, dim3(kRedThreads), 0, s, a, D, (int)units); break;
+    case 4: e = launch_pdl(splitk_reduce_kernel<4>, grid, dim3(kRedThreads), 0, s, a, D, (int)units); break;
+    default: e = launch_pdl(splitk_reduce_kernel<8>, grid, dim3(kRedThreads), 0, s, a, D, (int)units); break;
+  }
+  return check_cuda(e, "splitk_reduce launch");
 }
 
 // Split-K reduce with the output all-gather fused in.  A unit is (query row,
@@ -1032,7 +1140,9 @@ static int decode_impl(
     int32_t n_seqs, int32_t n_query_rows, int32_t max_queries_per_seq, int32_t max_ctx_len,
     int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim, float score_scale,
     int32_t partition_tokens, void* workspace, int64_t workspace_bytes_, int32_t* dev_status,
-    void* stream, const GatherArgs* gather) {
+    void* stream, const GatherArgs* gather, int32_t out_dtype) {
+  if (out_dtype != CLOVER_B200_F32 && out_dtype != CLOVER_B200_F16 && out_dtype != CLOVER_B200_BF16)
+    return set_error(CLOVER_B200_ERR_UNSUPPORTED, "paged_decode: out dtype %d", out_dtype);
   if (table_stride <= 0 || num_blocks <= 0)
     return set_error(CLOVER_B200_ERR_INVALID_ARG, "paged_decode: bad sizes");
   DecodePlan pl;
@@ -1071,6 +1181,7 @@ static int decode_impl(
   a.q = q;
   a.q_stride = q_row_stride;
   a.q_dtype = q_dtype;
+  a.out_dtype = out_dtype;
   a.k_cache = k_cache;
   a.v_cache = v_cache;
   a.tables = block_tables;
@@ -1191,10 +1302,7 @@ static int decode_impl(
     // Rows with several partitions are combined here; single-partition rows
     // were written by the decode kernel and return at once (the stream
     // kernel also leaves the empty rows' zeros to this kernel).
-    const dim3 rgrid(n_query_rows, num_q_heads, (head_dim + kReduceDims - 1) / kReduceDims);
-    rc = check_cuda(launch_pdl(splitk_reduce_kernel, rgrid, dim3(kReduceWarps * 32), 0, s, a,
-                               head_dim),
-                    "splitk_reduce launch");
+    rc = launch_splitk_reduce(a, head_dim, n_query_rows, s);
   }
   return rc;
 }
@@ -1213,7 +1321,7 @@ extern "C" int clover_b200_paged_decode(
                      seq_rows, query_start_loc, ctx_lens, n_seqs, n_query_rows,
                      max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads, head_dim,
                      score_scale, partition_tokens, workspace, workspace_bytes_, dev_status, stream,
-                     nullptr);
+                     nullptr, q_dtype);
 }
 
 extern "C" int clover_b200_decode_step(
@@ -1232,7 +1340,7 @@ extern "C" int clover_b200_decode_step(
                      table_stride, seq_rows, query_start_loc, ctx_lens, n_seqs, n_query_rows,
                      max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads, head_dim,
                      score_scale, partition_tokens, workspace, workspace_bytes_, dev_status, stream,
-                     nullptr);
+                     nullptr, q_dtype);
 }
 
 extern "C" int64_t clover_b200_decode_gather_workspace_bytes(
@@ -1249,15 +1357,15 @@ extern "C" int64_t clover_b200_decode_gather_workspace_bytes(
 
 extern "C" int64_t clover_b200_gather_sync_bytes(void) { return (int64_t)kSyncInts * 4; }
 
-extern "C" int clover_b200_decode_step_gather(
-    void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride, int32_t q_dtype,
-    void* k_cache, void* v_cache, int32_t kv_dtype, int64_t num_blocks, int32_t block_size,
-    const void* k_new, const void* v_new, int64_t new_token_stride, const int32_t* block_tables,
-    int32_t table_stride, const int32_t* seq_rows, const int32_t* query_start_loc,
-    const int32_t* ctx_lens, int32_t n_seqs, int32_t n_query_rows, int32_t max_queries_per_seq,
-    int32_t max_ctx_len, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
-    float score_scale, int32_t partition_tokens, void* const* peer_recv, int32_t* sync,
-    int32_t n_ranks, int32_t rank, int64_t recv_half_words, void* workspace,
+static int step_gather_impl(
+    void* out, int64_t out_row_stride, int32_t out_dtype, const void* q, int64_t q_row_stride,
+    int32_t q_dtype, void* k_cache, void* v_cache, int32_t kv_dtype, int64_t num_blocks,
+    int32_t block_size, const void* k_new, const void* v_new, int64_t new_token_stride,
+    const int32_t* block_tables, int32_t table_stride, const int32_t* seq_rows,
+    const int32_t* query_start_loc, const int32_t* ctx_lens, int32_t n_seqs, int32_t n_query_rows,
+    int32_t max_queries_per_seq, int32_t max_ctx_len, int32_t num_q_heads, int32_t num_kv_heads,
+    int32_t head_dim, float score_scale, int32_t partition_tokens, void* const* peer_recv,
+    int32_t* sync, int32_t n_ranks, int32_t rank, int64_t recv_half_words, void* workspace,
     int64_t workspace_bytes_, int32_t* dev_status, void* stream) {
   const int64_t total_q_heads = (int64_t)num_q_heads * n_ranks;
   if (!out || !peer_recv || !sync || n_ranks <= 0 || rank < 0 || rank >= n_ranks ||
@@ -1277,6 +1385,43 @@ extern "C" int clover_b200_decode_step_gather(
                      num_blocks, block_size, k_new, v_new, new_token_stride, block_tables,
                      table_stride, seq_rows, query_start_loc, ctx_lens, n_seqs, n_query_rows,
                      max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads, head_dim,
-                     score_scale, gather_partition(partition_tokens), workspace, workspace_bytes_, dev_status, stream,
-                     &g);
+                     score_scale, gather_partition(partition_tokens), workspace, workspace_bytes_,
+                     dev_status, stream, &g, out_dtype);
+}
+
+extern "C" int clover_b200_decode_step_gather(
+    void* out, int64_t out_row_stride, const void* q, int64_t q_row_stride, int32_t q_dtype,
+    void* k_cache, void* v_cache, int32_t kv_dtype, int64_t num_blocks, int32_t block_size,
+    const void* k_new, const void* v_new, int64_t new_token_stride, const int32_t* block_tables,
+    int32_t table_stride, const int32_t* seq_rows, const int32_t* query_start_loc,
+    const int32_t* ctx_lens, int32_t n_seqs, int32_t n_query_rows, int32_t max_queries_per_seq,
+    int32_t max_ctx_len, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+    float score_scale, int32_t partition_tokens, void* const* peer_recv, int32_t* sync,
+    int32_t n_ranks, int32_t rank, int64_t recv_half_words, void* workspace,
+    int64_t workspace_bytes_, int32_t* dev_status, void* stream) {
+  return step_gather_impl(out, out_row_stride, q_dtype, q, q_row_stride, q_dtype, k_cache, v_cache,
+                          kv_dtype, num_blocks, block_size, k_new, v_new, new_token_stride,
+                          block_tables, table_stride, seq_rows, query_start_loc, ctx_lens, n_seqs,
+                          n_query_rows, max_queries_per_seq, max_ctx_len, num_q_heads, num_kv_heads,
+                          head_dim, score_scale, partition_tokens, peer_recv, sync, n_ranks, rank,
+                          recv_half_words, workspace, workspace_bytes_, dev_status, stream);
+}
+
+extern "C" int clover_b200_decode_step_gather_into(
+    void* out, int64_t out_row_stride, int32_t out_dtype, const void* q, int64_t q_row_stride,
+    int32_t q_dtype, void* k_cache, void* v_cache, int32_t kv_dtype, int64_t num_blocks,
+    int32_t block_size, const void* k_new, const void* v_new, int64_t new_token_stride,
+    const int32_t* block_tables, int32_t table_stride, const int32_t* seq_rows,
+    const int32_t* query_start_loc, const int32_t* ctx_lens, int32_t n_seqs, int32_t n_query_rows,
+    int32_t max_queries_per_seq, int32_t max_ctx_len, int32_t num_q_heads, int32_t num_kv_heads,
+    int32_t head_dim, float score_scale, int32_t partition_tokens, void* const* peer_recv,
+    int32_t* sync, int32_t n_ranks, int32_t rank, int64_t recv_half_words, void* workspace,
+    int64_t workspace_bytes_, int32_t* dev_status, void* stream) {
+  return step_gather_impl(out, out_row_stride, out_dtype, q, q_row_stride, q_dtype, k_cache,
+                          v_cache, kv_dtype, num_blocks, block_size, k_new, v_new,
+                          new_token_stride, block_tables, table_stride, seq_rows, query_start_loc,
+                          ctx_lens, n_seqs, n_query_rows, max_queries_per_seq, max_ctx_len,
+                          num_q_heads, num_kv_heads, head_dim, score_scale, partition_tokens,
+                          peer_recv, sync, n_ranks, rank, recv_half_words, workspace,
+                          workspace_bytes_, dev_status, stream);
 }

@@ -206,9 +206,12 @@ class PagedKVPool:
     def decode_step_gather(self, layer: int, q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
                            query_start_loc: torch.Tensor, ctx_lens: torch.Tensor,
                            seq_rows: Optional[torch.Tensor], max_q: int, max_ctx: int,
-                           score_scale: float, gather, partition_tokens: int = 0) -> torch.Tensor:
+                           score_scale: float, gather, partition_tokens: int = 0,
+                           out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """decode_step for a head-sharded group: the all-gathered output of
-        every rank lands in ``gather.out`` (returned view, valid until the next call)."""
+        every rank lands in ``out`` ([rows, Hq_total, D] view of a consumer
+        buffer, any f32/f16/bf16) or in ``gather.out`` (returned view, valid
+        until the next call)."""
         n_seqs = query_start_loc.numel() - 1
         nbytes = _lib.decode_gather_workspace_bytes(n_seqs, q.shape[0], max_q, max_ctx, q.shape[1],
                                                     self.num_kv_heads, self.head_dim,
@@ -218,8 +221,8 @@ class PagedKVPool:
                                 query_start_loc, ctx_lens, gather, max_queries_per_seq=max_q,
                                 max_ctx_len=max_ctx, score_scale=score_scale, seq_rows=seq_rows,
                                 partition_tokens=partition_tokens, workspace=self.workspace(nbytes),
-                                status=self.status)
-        return gather.out[:q.shape[0]]
+                                status=self.status, out=out)
+        return gather.out[:q.shape[0]] if out is None else out
 
     # ------------------------------------------------------------ checks / views
     def check_status(self) -> None:

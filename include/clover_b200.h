@@ -341,6 +341,32 @@ CLOVER_B200_API int clover_b200_decode_step_gather(void* out, int64_t out_row_st
                              int32_t* dev_status, void* stream);
 
 /*
+ * clover_b200_decode_step_gather writing the all-gathered output in out_dtype
+ * (F32, F16 or BF16, independent of q_dtype) into a caller-given consumer
+ * buffer: row r of out (row stride out_row_stride elements) receives the
+ * [total_q_heads * head_dim] context of query row r, e.g. the dense node's
+ * o_proj input [rows, hidden] in the model's dtype.  Every other argument and
+ * result as clover_b200_decode_step_gather.
+ * Replaces: the hand-off of the gathered contexts to the dense node, which
+ * reshapes them into its o_proj input (src/core/scheduler.py:1058-1059,
+ * src/core/model_adapter.py:572).
+ */
+CLOVER_B200_API int clover_b200_decode_step_gather_into(void* out, int64_t out_row_stride,
+                             int32_t out_dtype, const void* q, int64_t q_row_stride, int32_t q_dtype,
+                             void* k_cache, void* v_cache, int32_t kv_dtype,
+                             int64_t num_blocks, int32_t block_size,
+                             const void* k_new, const void* v_new, int64_t new_token_stride,
+                             const int32_t* block_tables, int32_t table_stride,
+                             const int32_t* seq_rows, const int32_t* query_start_loc,
+                             const int32_t* ctx_lens, int32_t n_seqs, int32_t n_query_rows,
+                             int32_t max_queries_per_seq, int32_t max_ctx_len,
+                             int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                             float score_scale, int32_t partition_tokens,
+                             void* const* peer_recv, int32_t* sync, int32_t n_ranks, int32_t rank,
+                             int64_t recv_half_words, void* workspace, int64_t workspace_bytes,
+                             int32_t* dev_status, void* stream);
+
+/*
  * Allocation-free paged decode.  No counterpart in the upstream project: it
  * exists for callers that cannot call cudaMalloc (a serving engine that owns
  * all of HBM through its own pool, or a foreign-function host without a CUDA

@@ -124,6 +124,18 @@ def _worker(rank, world, port, q_out):
             errs.append(max(float((x - y).abs().max()) for x, y in zip(o0, o1)))
         assert bes[1]._peer is not None
         assert all(p.graphs for p in bes[1]._fast.values())  # the sharded step was captured
+        # the fused gather straight into a bf16 consumer buffer (the o_proj input)
+        qd = torch.randn(2, hq, D, generator=gen).bfloat16().float().to(dev)
+        knd = torch.randn(2, hkv, D, generator=gen).bfloat16().to(dev)
+        vnd = torch.randn(2, hkv, D, generator=gen).bfloat16().to(dev)
+        consumer = torch.zeros(2, 1, hq * D, dtype=torch.bfloat16, device=dev)
+        o_ref = bes[0].decode_batch(["a", "b"], 0, qd, knd, vnd, 1 / math.sqrt(D))
+        o_sh = bes[1].decode_batch(["a", "b"], 0, qd, knd, vnd, 1 / math.sqrt(D), out=consumer)
+        torch.cuda.synchronize(dev)
+        assert o_sh.data_ptr() == consumer.data_ptr()
+        # bf16 output: within half a bf16 ulp of the fp32 single-GPU result (+ the fp32 bound)
+        dev_err = (consumer.view(2, hq, D).float() - o_ref).abs() - o_ref.abs() * 2.0 ** -8
+        errs.append(max(0.0, float(dev_err.max())))
         bes[1].close()
         q_out.put((rank, int(st.item()), errs))
     except Exception as e:
