@@ -622,7 +622,12 @@ def run_e2e(cfg, lens, n_new, rank, world, device, args):
         qh = torch.randn((T, cfg.num_q_heads, D), generator=hg).pin_memory()
         kh = torch.randn((T, cfg.num_kv_heads, D), generator=hg).to(dt).pin_memory()
         vh = torch.randn((T, cfg.num_kv_heads, D), generator=hg).to(dt).pin_memory()
-        call = lambda: be.decode_batch(ids, 0, qh, kh, vh, cfg.score_scale, n_new=n_new).cpu()  # noqa: E731
+        def call():
+            # the output back into pinned host memory, then one stream sync
+            out = be.decode_batch(ids, 0, qh, kh, vh, cfg.score_scale, n_new=n_new)
+            host = out.to("cpu", non_blocking=True)
+            torch.cuda.current_stream(device).synchronize()
+            return host
     esz = torch.empty((), dtype=dt).element_size()
     h2d = T * cfg.num_q_heads * D * 4 + 2 * T * cfg.num_kv_heads * D * esz
     d2h = T * cfg.num_q_heads * D * 4

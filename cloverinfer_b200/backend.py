@@ -405,9 +405,14 @@ class B200AttentionBackend:
             return
         if self._pending_ingest:
             self._await_ingest()
-        rows, targets = self._plan_single(reqs, layer, q0.shape)
+        rows, targets, need = self._plan_single(reqs, layer, q0.shape)
         plan.meta[:] = rows + plan.offs_list + targets
         _lib.host_gather(srcs, plan.sizes, plan.n, plan.host.data_ptr())
+        if need:
+            # rows and new contexts (the targets) go to the device once, where
+            # the reserve kernel reads them ahead of the step
+            plan.dev[plan.m_off:].copy_(plan.host[plan.m_off:], non_blocking=True)
+            self.pool.commit_reserve(rows, targets, need, plan.rows, plan.ctx)
         pt = self._split(targets, _ONE)
         step = self._step_graph(plan, layer, scale, max(targets), pt) if plan.warm else None
         if step is not None:
@@ -440,8 +445,10 @@ class B200AttentionBackend:
         results[base:base + B] = plan.out.clone().split(1)
 
     def _plan_single(self, reqs, layer: int, q_shape):
-        """_plan for one new token per request: validate, reserve the blocks
-        the new tokens need; returns (table rows, contexts after the step)."""
+        """_plan for one new token per request: validate and count the blocks
+        the new tokens need (raising before any state changes when they do
+        not fit); returns (table rows, contexts after the step, blocks to
+        reserve).  The caller reserves them from the staged metadata."""
         pool = self.pool
         if not 0 <= layer < self.num_layers:
             raise IndexError(f"layer_idx {layer} out of range [0, {self.num_layers})")
@@ -455,9 +462,11 @@ class B200AttentionBackend:
         # (rows are distinct: decode_layer_batch never puts one request twice in a group)
         for r, t in zip(rows, targets):
             if t > blocks[r] * cap:  # some row crosses into a new block
-                pool.reserve(rows, targets, "OOM during append")
-                break
-        return rows, targets
+                need = pool.demand(rows, targets)
+                if need > pool.free_count:
+                    raise RuntimeError("OOM during append")
+                return rows, targets, need
+        return rows, targets, 0
 
     # Context lengths are rounded up to this many tokens for a captured step:
     # the launch's max_ctx_len (and so its partition plan and workspace) is

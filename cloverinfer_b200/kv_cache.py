@@ -127,14 +127,20 @@ class PagedKVPool:
             raise RuntimeError(oom_message)
         if need == 0:
             return 0
-        rd = to_device_i32(rows, self.device)
-        td = to_device_i32(targets, self.device)
-        _lib.block_reserve(self.free_stack, self.free_top, self.tables, self.table_len, rd, td,
-                           self.block_size, self.status)
+        self.commit_reserve(rows, targets, need, to_device_i32(rows, self.device),
+                            to_device_i32(targets, self.device))
+        return need
+
+    def commit_reserve(self, rows: Sequence[int], targets: Sequence[int], need: int,
+                       rows_d: torch.Tensor, targets_d: torch.Tensor) -> None:
+        """The reserve kernel for a batch already checked with ``demand`` (``need``
+        blocks, at most ``free_count``), reading rows and targets from device
+        int32 tensors the caller staged; then the host counters."""
+        _lib.block_reserve(self.free_stack, self.free_top, self.tables, self.table_len, rows_d,
+                           targets_d, self.block_size, self.status)
         for r, t in zip(rows, targets):
             self.row_blocks[r] = max(self.row_blocks[r], self.blocks_for(t))
         self.free_count -= need
-        return need
 
     def release(self, rows: Sequence[int]) -> None:
         rows = [r for r in rows if self.row_blocks[r] > 0]
