@@ -57,8 +57,9 @@ METRIC = "paged decode-attn KV-read GB/s"
 # paged_decode_mma_kernel launch from an ncu capture of the same workload and
 # kernel build: (config, GPUs, KV dtype option) -> (bytes, summary file).
 NCU_TRAFFIC = {
-    ("c3", 1, "config"): (1.0740e9 + 8.032e6, "profiles/paged_decode_mma_c3_full.md"),
-    ("c3", 8, "config"): (134.363e6 + 3.985e6, "profiles/paged_decode_mma_c3_shard8_full.md"),
+    ("c3", 1, "config"): (1.074150e9 + 9.415e6, "profiles/paged_decode_mma_c3_full.md"),
+    ("c3", 8, "config"): (134.347e6 + 4.144e6, "profiles/paged_decode_mma_c3_shard8_full.md"),
+    ("c4", 1, "config"): (2.323797e9 + 27.557e6, "profiles/paged_decode_mma_c4_full.md"),
 }
 
 
