@@ -353,8 +353,20 @@ def run_profile_share(args):
         st["decode_only"]()
     torch.cuda.synchronize()
     st["pool"].check_status()
+    msg = ""
+    if args.time_share:
+        # the share's decode (+ reduce) back to back in one graph, as the timed
+        # step chains them (no gather: a single GPU)
+        stream = torch.cuda.Stream(dev)
+        g = _capture(st["decode_only"], args.launches, stream)
+        with torch.cuda.stream(stream):
+            g.replay()
+        torch.cuda.synchronize()
+        reps = _replay_ms(g, stream, args.replays, args.launches)
+        g.reset()
+        msg = f", per launch {1e3 * statistics.median(reps):.2f} us (median of {len(reps)} replays)"
     print(f"{cfg.name}: rank {args.profile_rank}/{args.profile_share}, {st['hkv_local']} KV heads, "
-          f"partition {st['partition_tokens']} tokens, {args.launches} launches ok")
+          f"partition {st['partition_tokens']} tokens, {args.launches} launches ok{msg}")
 
 
 def _step_runner(st, world, T, cfg, device):
@@ -682,6 +694,8 @@ def main():
                     help="ncu case: one rank's share of a W-way shard on one GPU (no JSON)")
     ap.add_argument("--profile-rank", type=int, default=0)
     ap.add_argument("--launches", type=int, default=6)
+    ap.add_argument("--time-share", action="store_true",
+                    help="with --profile-share: also time the launches chained in one graph")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.profile_share:

@@ -210,7 +210,6 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   __shared__ __align__(8) uint64_t bars[NW * STAGES];
   __shared__ int s_abort;
 
-  pdl_wait();  // inputs, tables and workspace are final before anything is read
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   // The prologue takes three dependent memory round trips before the first
@@ -218,6 +217,13 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   // contexts and the block ids of the whole partition (ids past the context
   // are loaded but never used), (3) the first copies, with the queries
   // loaded alongside (an empty partition exits before loading them).
+  //
+  // (1) and (2) read only the step's metadata — rows, contexts, block
+  // tables — which no kernel that triggers this launch early writes (the
+  // split-K reduces write outputs and status words): they run before
+  // griddepcontrol.wait, under the previous kernel's tail.  Everything the
+  // preceding work may produce — queries, new K/V, cache contents,
+  // workspace — is read, and every write is made, after it.
   CtaWork w;
   w.b = blockIdx.z;
   w.p = blockIdx.x;
@@ -231,7 +237,10 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   w.tab = a.tables + (int64_t)trow * a.table_stride;
   w.tok_begin = w.p * a.part_tokens;
   const int c0 = w.chunk * G::kCols;
+  // (Every CTA waits before it ends, early exits too: a grid that finished
+  // before its predecessor would let the next kernel's wait pass early.)
   if ((stat & CLOVER_B200_DEV_TIMEOUT) || w.nq <= 0 || c0 >= w.nq * a.group) {
+    pdl_wait();
     pdl_trigger();
     return;
   }
@@ -258,6 +267,7 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
     ctx_end = a.max_parts * a.part_tokens;
   }
   if (w.tok_begin >= ctx_end) {
+    pdl_wait();
     if (w.p == 0) zero_empty_columns(a, w, D);
     pdl_trigger();
     return;
@@ -278,6 +288,7 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
       my_blk[i] = -1;
     }
   }
+  pdl_wait();  // queries, new K/V, cache contents and workspace are final from here
   if (a.k_new != nullptr && append_new_tokens(a, w, D)) fence_proxy_async_global();
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -668,8 +679,18 @@ splitk_reduce_kernel(const DecodeArgs a, int D, int n_units) {
   __shared__ float s_o[kReduceWarps][32 * EPL];
   __shared__ int s_unit[kRedThreads], s_npp[kRedThreads];
   __shared__ int s_n;
-  pdl_wait();     // every partial of the decode kernel is written
-  pdl_trigger();  // the next step's kernel may start launching (it waits too)
+  // The partition kernels' partial counts follow from the contexts alone, so
+  // the first screening round runs before griddepcontrol.wait; the balanced
+  // split's counts are written by the decode and are read after it.
+  bool waited = false;
+  auto wait_decode = [&]() {
+    if (!waited) {
+      pdl_wait();     // every partial of the decode kernel is written
+      pdl_trigger();  // the next step's kernel may start launching (it waits too)
+      waited = true;
+    }
+  };
+  if (a.part_count != nullptr) wait_decode();
   const int tid = threadIdx.x;
   const int H = a.num_q_heads;
   for (int64_t round = 0;; ++round) {
@@ -693,6 +714,7 @@ splitk_reduce_kernel(const DecodeArgs a, int D, int n_units) {
     }
     __syncthreads();
     const int n = s_n;
+    if (n > 0) wait_decode();
     for (int i = 0; i < n; ++i) {
       const int u = s_unit[i];
       const int r = u / H, h = u - r * H;
@@ -700,6 +722,7 @@ splitk_reduce_kernel(const DecodeArgs a, int D, int n_units) {
     }
     __syncthreads();  // everyone read s_n before the next round resets it
   }
+  wait_decode();  // (a CTA with nothing to reduce still lets the next kernel launch)
 }
 
 static int launch_splitk_reduce(const DecodeArgs& a, int D, int n_rows, cudaStream_t s) {

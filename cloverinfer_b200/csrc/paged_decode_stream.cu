@@ -200,11 +200,18 @@ paged_decode_stream_kernel(const __grid_constant__ CUtensorMap tmK,
   __shared__ int s_wsum[E][NW];
   __shared__ int s_start[NW][2];
 
-  pdl_wait();  // inputs, tables and workspace are final before anything is read
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  // The plan and the first batches of block ids read only the step's
+  // metadata (rows, contexts, block tables), which no kernel that triggers
+  // this launch early writes: they run before griddepcontrol.wait, under the
+  // previous kernel's tail.  Queries, new K/V, cache contents and workspace
+  // are read, and every write made, after it.
   // After a bounded wait gave up anywhere, later launches stop at once.
+  // (Every CTA waits before it ends, early exits too: a grid that finished
+  // before its predecessor would let the next kernel's wait pass early.)
   if (a.status != nullptr && (*(volatile int32_t*)a.status & CLOVER_B200_DEV_TIMEOUT)) {
+    pdl_wait();
     pdl_trigger();
     return;
   }
@@ -273,6 +280,7 @@ paged_decode_stream_kernel(const __grid_constant__ CUtensorMap tmK,
   const int u0 = wid * per;
   const int n_units = u0 < U ? (U - u0 < per ? U - u0 : per) : 0;
   if (n_units == 0 || s_start[warp][0] < 0) {
+    pdl_wait();
     pdl_trigger();
     return;
   }
@@ -397,6 +405,7 @@ paged_decode_stream_kernel(const __grid_constant__ CUtensorMap tmK,
     c.reset();
   };
 
+  pdl_wait();  // queries, new K/V, cache contents and workspace are final from here
   // First copies in flight, then the first piece's queries and limits load
   // while they land.
   const int npre = n_units < STAGES ? n_units : STAGES;
