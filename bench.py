@@ -238,17 +238,23 @@ def build_step(cfg, rank, world, lens, device, seed=0, gather=None, n_new=None, 
                              partition_tokens=partition_tokens)
 
 
-def _replay_ms(graph, stream, replays: int, steps: int):
-    """Per-step ms of `replays` individually timed replays of a `steps`-step graph."""
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(replays)]
-    with torch.cuda.stream(stream):
-        for e0, e1 in evs:
-            e0.record(stream)
-            graph.replay()
-            e1.record(stream)
-    torch.cuda.synchronize()
-    return [a.elapsed_time(b) / steps for a, b in evs]
+def _replay_ms(graph, stream, replays: int, steps: int, min_seconds: float = 0.0):
+    """Per-step ms of individually timed replays of a `steps`-step graph: at
+    least `replays` of them, and more until `min_seconds` have passed (so the
+    clock sampler sees the GPU under load)."""
+    out = []
+    t0 = time.perf_counter()
+    while len(out) < replays or time.perf_counter() - t0 < min_seconds:
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(replays)]
+        with torch.cuda.stream(stream):
+            for e0, e1 in evs:
+                e0.record(stream)
+                graph.replay()
+                e1.record(stream)
+        torch.cuda.synchronize()
+        out += [a.elapsed_time(b) / steps for a, b in evs]
+    return out
 
 
 def _spread(ms):
@@ -472,8 +478,12 @@ def run_b200(args):
     spread = None
     if graph is not None:
         _barrier(world)
-        reps = _replay_ms(graph, stream, args.replays, args.steps)
-        spread = _spread([_max_over_ranks(x, world) for x in reps])
+        reps = _replay_ms(graph, stream, args.replays, args.steps, min_seconds=1.0)
+        # every rank times the same number of replays: the max is taken replay by replay
+        n = int(_max_over_ranks(float(len(reps)), world))
+        while len(reps) < n:
+            reps += _replay_ms(graph, stream, 1, args.steps)
+        spread = _spread([_max_over_ranks(x, world) for x in reps[:n]])
 
     # Dominant kernel alone: decode (+ its split-K reduce) launches back to back
     # in one graph, timed between CUDA events on the launching stream (median
