@@ -84,6 +84,9 @@ struct DecodeArgs {
   int32_t n_seqs;
   int32_t max_ctx;
   int32_t max_q;
+  // One query row per sequence (max_q == 1 and as many rows as sequences):
+  // query_start_loc is then the identity and the kernels do not load it.
+  int32_t rows_identity;
   int32_t min_units;
   int32_t* part_count;
   // Limit of this launch's bounded waits (wait_limit_ns() at launch).

@@ -229,8 +229,8 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   w.p = blockIdx.x;
   w.kvh = blockIdx.y / a.col_chunks;
   w.chunk = blockIdx.y - w.kvh * a.col_chunks;
-  w.row0 = __ldg(a.qsl + w.b);
-  w.nq = __ldg(a.qsl + w.b + 1) - w.row0;
+  w.row0 = a.rows_identity ? w.b : __ldg(a.qsl + w.b);
+  w.nq = a.rows_identity ? 1 : __ldg(a.qsl + w.b + 1) - w.row0;
   const int trow = a.seq_rows ? __ldg(a.seq_rows + w.b) : w.b;
   // after a bounded wait gave up anywhere, later CTAs stop at once
   const int stat = a.status != nullptr ? *(volatile int32_t*)a.status : 0;
@@ -606,21 +606,14 @@ __device__ __forceinline__ float reduce_unit(const DecodeArgs& a, int r, int h, 
   return v;
 }
 
-// Split-K reduce for paged_decode / decode_step.  A unit is one (query row,
-// head); a CTA of 4 warps first screens up to 128 of its units at once (one
-// round trip for their contexts or part counts) and then reduces only those
-// with several partials: the CTA's threads take the log-sum-exp values (max,
-// then the sum of the weights), then warp w adds partitions w, w + 4, ...
-// of every dim (lane l: dims l, l + 32, ...; 8 partitions' loads in flight),
-// and the four warp sums are added in shared memory.  Units the decode wrote
-// itself (one partition) cost only the screening load, so a ragged batch
-// whose rows mostly fit one partition launches no CTA per (row, head).
 constexpr int kRedThreads = kReduceWarps * 32;
-constexpr int kRedBatch = 8;  // partitions per warp in flight
 
-template <int EPL>
-__device__ __forceinline__ void reduce_rows_unit(const DecodeArgs& a, int r, int h, int npp,
-                                                 int D, float* s_red, float (*s_o)[32 * EPL]) {
+// One unit: (row r, head h, dims [d0, d0 + 32 EPL) of D); warp w adds
+// partitions w, w + 4, ..., BATCH of them in flight.
+template <int EPL, int BATCH>
+__device__ __forceinline__ void reduce_rows_unit(const DecodeArgs& a, int r, int h, int d0,
+                                                 int npp, int D, float* s_red,
+                                                 float (*s_o)[32 * EPL]) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t base = ((int64_t)r * a.num_q_heads + h) * a.max_parts;
   // (1) max and sum of the weights 2^(lse_p - M) over the partitions
@@ -641,21 +634,21 @@ __device__ __forceinline__ void reduce_rows_unit(const DecodeArgs& a, int r, int
   float acc[EPL];
 #pragma unroll
   for (int j = 0; j < EPL; ++j) acc[j] = 0.f;
-  for (int p0 = warp; p0 < npp; p0 += kReduceWarps * kRedBatch) {
-    float wv[kRedBatch], v[kRedBatch][EPL];
+  for (int p0 = warp; p0 < npp; p0 += kReduceWarps * BATCH) {
+    float wv[BATCH], v[BATCH][EPL];
 #pragma unroll
-    for (int i = 0; i < kRedBatch; ++i) {
+    for (int i = 0; i < BATCH; ++i) {
       const int p = p0 + i * kReduceWarps;
       const bool ok = p < npp;
       wv[i] = ok ? __ldcg(a.part_lse + base + p) : -INFINITY;
 #pragma unroll
       for (int j = 0; j < EPL; ++j) {
-        const int d = lane + 32 * j;
+        const int d = d0 + lane + 32 * j;
         v[i][j] = (ok && d < D) ? __ldcg(a.part_out + (base + p) * D + d) : 0.f;
       }
     }
 #pragma unroll
-    for (int i = 0; i < kRedBatch; ++i) {
+    for (int i = 0; i < BATCH; ++i) {
       const float wi = fast_exp2(wv[i] - u);
 #pragma unroll
       for (int j = 0; j < EPL; ++j) acc[j] = fmaf(wi, v[i][j], acc[j]);
@@ -665,14 +658,28 @@ __device__ __forceinline__ void reduce_rows_unit(const DecodeArgs& a, int r, int
   for (int j = 0; j < EPL; ++j) s_o[warp][lane + 32 * j] = acc[j];
   __syncthreads();
   const float L = s_red[4] + s_red[5] + s_red[6] + s_red[7];
-  for (int d = tid; d < D; d += kRedThreads) {
-    const float o = s_o[0][d] + s_o[1][d] + s_o[2][d] + s_o[3][d];
+  for (int i = tid; i < 32 * EPL; i += kRedThreads) {
+    const int d = d0 + i;
+    if (d >= D) continue;
+    const float o = s_o[0][i] + s_o[1][i] + s_o[2][i] + s_o[3][i];
     store_out(a, (int64_t)r * a.out_stride + (int64_t)h * D + d, L > 0.f ? o / L : 0.f);
   }
   __syncthreads();  // shared scratch is reused by the next unit
 }
 
-template <int EPL>
+// Split-K reduce for paged_decode / decode_step.  A unit is one (query row,
+// head, 32 EPL dims); a CTA of 4 warps first screens up to 128 of its units
+// at once (one round trip for their contexts or part counts) and then
+// reduces only those with several partials: the CTA's threads take the
+// log-sum-exp values (max, then the sum of the weights), then warp w adds
+// partitions w, w + 4, ... (BATCH loads in flight per lane), and the four
+// warp sums are added in shared memory.  Units the decode wrote itself (one
+// partition) cost only the screening load, so a ragged batch whose rows
+// mostly fit one partition launches no CTA per (row, head).  Rows with up to
+// 16 partials take all dims per unit; rows with more take 32 dims per unit
+// and 32 partitions per warp in flight, so a few long rows still spread over
+// the SMs and need one round trip for their partials.
+template <int EPL, int BATCH>
 __global__ void __launch_bounds__(kRedThreads)
 splitk_reduce_kernel(const DecodeArgs a, int D, int n_units) {
   __shared__ float s_red[8];
@@ -693,6 +700,7 @@ splitk_reduce_kernel(const DecodeArgs a, int D, int n_units) {
   if (a.part_count != nullptr) wait_decode();
   const int tid = threadIdx.x;
   const int H = a.num_q_heads;
+  const int dch = (D + 32 * EPL - 1) / (32 * EPL);  // dim chunks per (row, head)
   for (int64_t round = 0;; ++round) {
     const int64_t first = (int64_t)blockIdx.x + round * kRedThreads * gridDim.x;
     if (first >= n_units) break;
@@ -701,7 +709,8 @@ splitk_reduce_kernel(const DecodeArgs a, int D, int n_units) {
     const int64_t uu = first + (int64_t)tid * gridDim.x;
     if (uu < n_units) {
       const int u = (int)uu;
-      const int r = u / H, h = u - r * H;
+      const int rh = u / dch;
+      const int r = rh / H, h = rh - r * H;
       const int npp = partial_count(a, r, h, __ldg(a.ctx + r));
       // Single-partition rows were written by the decode kernel, and so were
       // the empty rows of the partition kernels; the stream kernel leaves
@@ -717,8 +726,9 @@ splitk_reduce_kernel(const DecodeArgs a, int D, int n_units) {
     if (n > 0) wait_decode();
     for (int i = 0; i < n; ++i) {
       const int u = s_unit[i];
-      const int r = u / H, h = u - r * H;
-      reduce_rows_unit<EPL>(a, r, h, s_npp[i], D, s_red, s_o);
+      const int rh = u / dch, dc = u - rh * dch;
+      const int r = rh / H, h = rh - r * H;
+      reduce_rows_unit<EPL, BATCH>(a, r, h, dc * 32 * EPL, s_npp[i], D, s_red, s_o);
     }
     __syncthreads();  // everyone read s_n before the next round resets it
   }
@@ -726,22 +736,34 @@ splitk_reduce_kernel(const DecodeArgs a, int D, int n_units) {
 }
 
 static int launch_splitk_reduce(const DecodeArgs& a, int D, int n_rows, cudaStream_t s) {
-  const int64_t units = (int64_t)n_rows * a.num_q_heads;
-  if (units <= 0) return CLOVER_B200_OK;
-  if (units > INT32_MAX) return set_error(CLOVER_B200_ERR_UNSUPPORTED, "splitk_reduce: too many rows");
   int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess)
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // Few (row, head) pairs with many partials each (one KV head per GPU, long
+  // contexts): 32 dims per unit, one lane per dim and 32 partitions per warp
+  // in flight, so the pairs spread over the SMs (one rank's share of C3 at 8
+  // GPUs: 34.1 against 34.7 us for decode + reduce).  Otherwise every dim of
+  // a pair per unit (C3 on one GPU: 175.2 against 178.4 us).
+  const bool chunked = a.max_parts > 16 && (int64_t)n_rows * a.num_q_heads < sms;
+  const int epl = chunked ? 1 : (D + 31) / 32;
+  const int64_t units = (int64_t)n_rows * a.num_q_heads * ((D + 32 * epl - 1) / (32 * epl));
+  if (units <= 0) return CLOVER_B200_OK;
+  if (units > INT32_MAX) return set_error(CLOVER_B200_ERR_UNSUPPORTED, "splitk_reduce: too many rows");
   const int64_t cap = (int64_t)sms * 16;
   const dim3 grid((unsigned)(units < cap ? units : cap));
-  const int epl = (D + 31) / 32;
+  const dim3 block(kRedThreads);
+  const int nu = (int)units;
   cudaError_t e;
-  switch (epl) {
-    case 1: e = launch_pdl(splitk_reduce_kernel<1>, grid, dim3(kRedThreads), 0, s, a, D, (int)units); break;
-    case 2: e = launch_pdl(splitk_reduce_kernel<2>, grid, dim3(kRedThreads), 0, s, a, D, (int)units); break;
-    case 3: e = launch_pdl(splitk_reduce_kernel<3>, grid, dim3(kRedThreads), 0, s, a, D, (int)units); break;
-    case 4: e = launch_pdl(splitk_reduce_kernel<4>, grid, dim3(kRedThreads), 0, s, a, D, (int)units); break;
-    default: e = launch_pdl(splitk_reduce_kernel<8>, grid, dim3(kRedThreads), 0, s, a, D, (int)units); break;
+  if (chunked) {
+    e = launch_pdl(splitk_reduce_kernel<1, 32>, grid, block, 0, s, a, D, nu);
+  } else {
+    switch (epl) {
+      case 1: e = launch_pdl(splitk_reduce_kernel<1, 8>, grid, block, 0, s, a, D, nu); break;
+      case 2: e = launch_pdl(splitk_reduce_kernel<2, 8>, grid, block, 0, s, a, D, nu); break;
+      case 3: e = launch_pdl(splitk_reduce_kernel<3, 8>, grid, block, 0, s, a, D, nu); break;
+      case 4: e = launch_pdl(splitk_reduce_kernel<4, 8>, grid, block, 0, s, a, D, nu); break;
+      default: e = launch_pdl(splitk_reduce_kernel<8, 8>, grid, block, 0, s, a, D, nu); break;
+    }
   }
   return check_cuda(e, "splitk_reduce launch");
 }
@@ -1236,6 +1258,7 @@ static int decode_impl(
   a.n_seqs = n_seqs;
   a.max_ctx = max_ctx_len;
   a.max_q = max_queries_per_seq > 0 ? max_queries_per_seq : 1;
+  a.rows_identity = a.max_q == 1 && n_query_rows == n_seqs;
   a.min_units = kStreamMinUnits;
   a.part_count = nullptr;
   a.wait_ns = wait_limit_ns();

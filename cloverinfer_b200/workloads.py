@@ -149,8 +149,11 @@ def build_decode_step(cfg, rank, world, lens, device, seed=0, gather=None, n_new
     else:
         nbytes = _lib.decode_workspace_bytes(B, T, max_q, max(lens), hq_l, hkv_l, D, bs, dt, q.dtype, pt)
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+    # Table row b belongs to sequence b (reserved in order above): the tables are
+    # per sequence, as the reference's get_kernel_inputs lays them out
+    # (memory_manager.py:145-173), so the launches take no row indirection.
     common = dict(max_queries_per_seq=max_q, max_ctx_len=max(lens), score_scale=cfg.score_scale,
-                  seq_rows=rows, partition_tokens=pt, workspace=ws, status=pool.status)
+                  seq_rows=None, partition_tokens=pt, workspace=ws, status=pool.status)
 
     def decode_only():
         _lib.paged_decode(out, q, pool.k[0], pool.v[0], pool.tables, offs_d, ctx_d, **common)
