@@ -585,6 +585,14 @@ class B200AttentionBackend:
         if self._pending_ingest:
             self._await_ingest()
         dst = None if out is None else self._consumer_view(out, T, query.shape[1])
+        # host inputs start their (asynchronous, from pinned memory) copies now,
+        # so the planning below overlaps them
+        if not query.is_cuda:
+            query = query.to(self.device, non_blocking=True)
+        if not key.is_cuda:
+            key = key.to(self.device, non_blocking=True)
+        if not value.is_cuda:
+            value = value.to(self.device, non_blocking=True)
         reqs, rows, targets, offs, ctx_rows = self._plan(request_ids, layer_idx, n_new, query.shape[1:])
         meta = to_device_i32(rows + offs + ctx_rows, self.device)
         res = self._launch(reqs, layer_idx, n_new, targets, query, key, value, meta[0:B],
