@@ -354,7 +354,8 @@ def run_profile_share(args):
     lens = context_lengths(cfg, 0, args.batch)
     pt = args.partition_tokens if args.partition_tokens is not None else 0
     st = build_decode_step(cfg, args.profile_rank, args.profile_share, lens, dev,
-                           n_new=new_tokens(cfg, 0, args.batch), partition_tokens=pt)
+                           n_new=new_tokens(cfg, 0, args.batch), partition_tokens=pt,
+                           pool_blocks=0)  # a small device footprint for ncu's replays
     for _ in range(args.launches):
         st["decode_only"]()
     torch.cuda.synchronize()
@@ -560,7 +561,7 @@ def run_b200(args):
         "config": {"workload": cfg.name, "batch": B, "new_tokens": T, "ctx": f"{cfg.ctx_lo}-{cfg.ctx_hi}",
                    "num_q_heads": cfg.num_q_heads, "num_kv_heads": cfg.num_kv_heads,
                    "head_dim": cfg.head_dim, "block_size": cfg.block_size,
-                   "partition_tokens": st["partition_tokens"],
+                   "partition_tokens": st["partition_tokens"], "pool_blocks": st["pool_blocks"],
                    "split": ("balanced over all resident warps" if st["partition_tokens"] < 0
                              else "%d-token partitions" % st["partition_tokens"]),
                    "parallelism": f"kv-head-shard{world}", "gather": gather_kind,

@@ -99,12 +99,14 @@ def kv_bytes(ctx_per_seq: List[int], num_kv_heads: int, head_dim: int, dtype: to
 
 
 def build_decode_step(cfg, rank, world, lens, device, seed=0, gather=None, n_new=None,
-                      partition_tokens=0):
+                      partition_tokens=0, pool_blocks=None):
     """Pool + static buffers for one decode step: sequence b holds lens[b]
     tokens after the step, n_new[b] of them (default 1) appended by it and
     attended causally.  ``partition_tokens``: 0 leaves the split to the
     library, -1 asks for the balanced split, None takes the configuration's
-    fixed partition length on one GPU (the library's choice on several)."""
+    fixed partition length on one GPU (the library's choice on several).
+    ``pool_blocks``: None takes the configuration's pool size (capped at half
+    the device's free memory), 0 just the blocks the tables need."""
     from . import _lib
     from .head_groups import kv_head_shards
     from .kv_cache import PagedKVPool, auto_partition
@@ -116,14 +118,28 @@ def build_decode_step(cfg, rank, world, lens, device, seed=0, gather=None, n_new
     n_new = [1] * B if n_new is None else list(n_new)
     T = sum(n_new)
     blocks = sum(-(-n // bs) for n in lens) + 64
+    want = cfg.pool_blocks if pool_blocks is None else pool_blocks
+    if want > blocks and torch.device(device).type == "cuda":
+        # the configured pool (C4: 2M blocks), as far as half the free memory
+        # holds it; the shuffled free stack spreads the tables over all of it
+        esz = torch.empty((), dtype=dt).element_size()
+        per_block = 2 * bs * hkv_l * D * esz
+        free, _ = torch.cuda.mem_get_info(device)
+        blocks = max(blocks, min(want, int(0.5 * free) // per_block))
     pool = PagedKVPool(blocks, bs, hkv_l, D, num_layers=1, dtype=dt, device=device,
                        max_seqs=B, max_blocks_per_seq=max(-(-n // bs) for n in lens) + 1)
     pool.shuffle_free_stack(1234 + seed)
     pool.reserve(list(range(B)), list(lens))
     g = torch.Generator(device=device).manual_seed(4321 + rank)
+    chunk = 1 << 28
     for t in (pool.k, pool.v):  # fill the whole pool: every block holds N(0,1)*scale data
-        t.normal_(0.0, cfg.value_scale, generator=g) if dt == torch.float32 else \
-            t.copy_(torch.randn(t.shape, generator=g, device=device).mul_(cfg.value_scale).to(dt))
+        flat = t.view(-1)
+        for i in range(0, flat.numel(), chunk):
+            part = flat[i:i + chunk]
+            if dt == torch.float32:
+                part.normal_(0.0, cfg.value_scale, generator=g)
+            else:
+                part.copy_(torch.randn(part.numel(), generator=g, device=device).mul_(cfg.value_scale).to(dt))
     q = (torch.randn((T, hq_l, D), generator=g, device=device) * cfg.value_scale).to(dt).float()
     kn = (torch.randn((T, hkv_l, D), generator=g, device=device) * cfg.value_scale).to(dt)
     vn = (torch.randn((T, hkv_l, D), generator=g, device=device) * cfg.value_scale).to(dt)
@@ -169,5 +185,6 @@ def build_decode_step(cfg, rank, world, lens, device, seed=0, gather=None, n_new
 
     return dict(pool=pool, q=q, out=out, step=step, decode_only=decode_only, hkv_local=hkv_l,
                 hq_local=hq_l, kv_range=(lo, hi), partition_tokens=pt, workspace_bytes=nbytes,
-                rows=T, max_q=max_q, k_new=kn, v_new=vn, n_new=n_new, ctx_rows=ctx)
+                rows=T, max_q=max_q, k_new=kn, v_new=vn, n_new=n_new, ctx_rows=ctx,
+                pool_blocks=pool.num_blocks)
 
