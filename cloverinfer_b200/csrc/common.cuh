@@ -97,6 +97,23 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   }
 }
 
+// Named barrier ID over NTHREADS threads (whole warps) that also ORs a
+// predicate over them: every participant gets the same answer.  (Immediate
+// operands, so the kernel reserves only the barriers it names.)
+template <int ID, int NTHREADS>
+__device__ __forceinline__ bool bar_red_or(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "barrier.cta.red.or.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "n"(ID), "n"(NTHREADS)
+      : "memory");
+  return r != 0;
+}
+
 // --- TMA: 3-D tiled bulk tensor load global -> shared, completion on mbarrier.
 // (No multicast: every load lands in the issuing CTA's own shared memory.)
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int32_t x, int32_t y,

@@ -152,7 +152,11 @@ __device__ __forceinline__ void store_out(const DecodeArgs& a, int64_t idx, floa
 // a row (64 bf16/fp16 values, or 128 fp8 values) with the TMA 128-byte
 // swizzle.  An fp8 cache (F8) adds one fp16 staging stage (K and V) per warp
 // that each landed stage is converted into before the tensor-core step.
-template <int D, int BS, int NT = 1, bool F8 = false>
+//
+// CW > 1 (column warps): CW warps share each token warp's ring, each holding
+// its own NT n-tiles of the CTA's columns, so a CTA of kMmaWarps * CW warps
+// carries kCols * CW columns with the ring of kMmaWarps warps.
+template <int D, int BS, int NT = 1, bool F8 = false, int CW = 1>
 struct MmaGeom {
   static constexpr int kEsz = F8 ? 1 : 2;            // bytes per cached value
   static constexpr int kChunkVals = 128 / kEsz;       // values per 128-byte chunk
@@ -171,7 +175,9 @@ struct MmaGeom {
   static constexpr int kWarpBytes = kStages * kStage + kConv;
   static constexpr int kPipeBytes = kMmaWarps * kWarpBytes;
   static constexpr int kCols = kMmaCols * NT;  // columns per warp (NT n-tiles)
-  static constexpr int kRedBytes = kMmaWarps * kCols * (D + 4) * 4 + 2 * kMmaWarps * kCols * 4;
+  static constexpr int kCtaCols = kCols * CW;  // columns per CTA
+  static constexpr int kThreads = kMmaWarps * CW * 32;
+  static constexpr int kRedBytes = kMmaWarps * kCtaCols * (D + 4) * 4 + 2 * kMmaWarps * kCtaCols * 4;
   static constexpr int kSmem = (kPipeBytes > kRedBytes ? kPipeBytes : kRedBytes) + 1024;
 };
 
@@ -468,9 +474,10 @@ int stream_decode(int kv_dtype, int q_dtype, int D, int BS, int cols, const Deco
 // twice the accumulators (and run 3 CTAs per SM at block 32, whose stages
 // are twice as large); an fp8 cache's warps hold a deeper ring plus an fp16
 // staging stage (5 CTAs per SM).
-template <int D, int NT, bool F8 = false>
+// Column-split CTAs (CW = 2: four warps) run 3 per SM, 12 warps.
+template <int D, int NT, bool F8 = false, int CW = 1>
 constexpr int mma_min_ctas() {
-  return D >= 256 ? 1 : (NT > 1 ? 3 : (F8 ? 5 : CLOVER_MMA_MIN_CTAS));
+  return D >= 256 ? 1 : ((NT > 1 || CW > 1) ? 3 : (F8 ? 5 : CLOVER_MMA_MIN_CTAS));
 }
 
 }  // namespace clover

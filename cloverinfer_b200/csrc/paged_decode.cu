@@ -161,7 +161,7 @@ append_at_ctx_kernel(const DecodeArgs a, int D) {
 __device__ __forceinline__ void merge_store_rt(const DecodeArgs& a, const CtaWork& w,
                                                const float* red_acc, const float* red_m,
                                                const float* red_l, int cols, int D, int nw) {
-  for (int idx = threadIdx.x; idx < cols * D; idx += nw * 32) {
+  for (int idx = threadIdx.x; idx < cols * D; idx += blockDim.x) {
     const int col = idx / D;
     const int dim = idx - col * D;
     const ColInfo ci = col_info(a, w.row0, w.nq, w.kvh, w.chunk * a.cols_per_cta + col);
@@ -196,12 +196,14 @@ __device__ __forceinline__ void merge_store_rt(const DecodeArgs& a, const CtaWor
 }
 
 
-template <typename T, bool QF32, int D, int BS, int NT, bool F8>
-__global__ void __launch_bounds__(kMmaThreads, mma_min_ctas<D, NT, F8>())
+template <typename T, bool QF32, int D, int BS, int NT, bool F8, int CW>
+__global__ void __launch_bounds__(kMmaThreads * CW, mma_min_ctas<D, NT, F8, CW>())
 paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const DecodeArgs a) {
-  using G = MmaGeom<D, BS, NT, F8>;
-  constexpr int NW = kMmaWarps;
+  using G = MmaGeom<D, BS, NT, F8, CW>;
+  static_assert(CW == 1 || !F8, "column warps share 16-bit stages only");
+  constexpr int NW = kMmaWarps;  // token warps (one ring each)
+  constexpr int CCOLS = G::kCtaCols;
   constexpr int STAGES = G::kStages;
   constexpr int BPS = G::kBps;
   constexpr int TOK = G::kTok;
@@ -211,7 +213,12 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   __shared__ int s_abort;
 
   const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
+  // Warp (warp, cw): token warp `warp` owns a ring and issues its copies when
+  // cw == 0; its CW column warps all read the ring's stages, each for its
+  // own kCols columns, and agree on every stage (bar_red_or) before the slot
+  // is refilled.
+  const int warp = (threadIdx.x >> 5) % NW;
+  const int cw = (threadIdx.x >> 5) / NW;
   // The prologue takes three dependent memory round trips before the first
   // KV copy lands: (1) the sequence's rows and table row, (2) the rows'
   // contexts and the block ids of the whole partition (ids past the context
@@ -236,7 +243,7 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   const int stat = a.status != nullptr ? *(volatile int32_t*)a.status : 0;
   w.tab = a.tables + (int64_t)trow * a.table_stride;
   w.tok_begin = w.p * a.part_tokens;
-  const int c0 = w.chunk * G::kCols;
+  const int c0 = w.chunk * CCOLS;
   // (Every CTA waits before it ends, early exits too: a grid that finished
   // before its predecessor would let the next kernel's wait pass early.)
   if ((stat & CLOVER_B200_DEV_TIMEOUT) || w.nq <= 0 || c0 >= w.nq * a.group) {
@@ -253,13 +260,14 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
   for (int i = 0; i < BPS; ++i) {
     const int gi = (warp + lane * NW) * BPS + i;  // block index within the partition
     const int bi = blk0 + gi;
-    my_blk[i] = (warp + lane * NW < n_grp_full && gi * BS < a.part_tokens && bi < a.table_stride)
+    my_blk[i] = (cw == 0 && warp + lane * NW < n_grp_full && gi * BS < a.part_tokens &&
+                 bi < a.table_stride)
                     ? __ldg(w.tab + bi)
                     : -1;
   }
   // the longest causal limit among this chunk's rows bounds the token range
   const int j_lo = c0 / a.group;
-  const int j_hi = min(w.nq - 1, (c0 + G::kCols - 1) / a.group);
+  const int j_hi = min(w.nq - 1, (c0 + CCOLS - 1) / a.group);
   int ctx_end = 0;
   for (int j = j_lo; j <= j_hi; ++j) ctx_end = max(ctx_end, __ldg(a.ctx + w.row0 + j));
   if (ctx_end > a.max_parts * a.part_tokens) {
@@ -279,7 +287,7 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
 #pragma unroll
   for (int i = 0; i < BPS; ++i) {
     const int gi = (warp + lane * NW) * BPS + i;
-    if (lane < n_mine && gi < n_blk) {
+    if (cw == 0 && lane < n_mine && gi < n_blk) {
       if (my_blk[i] < 0 || my_blk[i] >= a.num_blocks) {
         raise_status(a.status, CLOVER_B200_DEV_BAD_BLOCK);
         my_blk[i] = 0;  // keep the pipeline well-formed; the output is flagged invalid
@@ -336,23 +344,25 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
 
   // First stages in flight, then the query fragments (MMA B operand) and the
   // causal limits of this thread's accumulator columns.
-  const int npre = n_mine < STAGES ? n_mine : STAGES;
+  const int npre = cw == 0 ? (n_mine < STAGES ? n_mine : STAGES) : 0;
   for (int k = 0; k < npre; ++k) issue(k);
   int issued = npre;
   int consumed = 0;
+  const int wc0 = c0 + cw * G::kCols;  // this warp's first column
+  const bool any_col = wc0 < w.nq * a.group;
   MmaCols<D, NT> c;
-  load_cols<T, QF32, D, NT>(a, w.row0, w.nq, w.kvh, c0, c, lane);
+  load_cols<T, QF32, D, NT>(a, w.row0, w.nq, w.kvh, wc0, c, lane);
   c.reset();
 
   bool timed_out = false;
 
   for (int k = 0; k < n_mine; ++k) {
     const int s = k % STAGES;
-    if (!mbar_wait_bounded(bar0 + s * 8, (k / STAGES) & 1, a.wait_ns)) {
+    const bool landed = mbar_wait_bounded(bar0 + s * 8, (k / STAGES) & 1, a.wait_ns);
+    if (CW == 1 && !landed) {
       timed_out = true;
       break;
     }
-    consumed = k + 1;
     uint32_t ks = ring + s * G::kStage;
     uint32_t vs = ks + G::kTile;
     if (F8) {
@@ -370,17 +380,30 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
       vs = conv + TOK * D * 2;
     }
     const int tok0 = w.tok_begin + (warp + k * NW) * TOK;
-    mma_stage<T, QF32, D, TOK, NT>(ks, vs, smem + (vs - smem_addr(smem)), tok0,
-                                   w.tok_end - tok0, a.scale_log2, c, lane);
-    __syncwarp();
-    if (!F8 && k + STAGES < n_mine) {
+    if (landed && any_col)
+      mma_stage<T, QF32, D, TOK, NT>(ks, vs, smem + (vs - smem_addr(smem)), tok0,
+                                     w.tok_end - tok0, a.scale_log2, c, lane);
+    if (CW > 1) {
+      // every column warp is done with the slot (or one gave up: all do)
+      static_assert(NW == 2, "one named barrier per token warp");
+      const bool fail = warp == 0 ? bar_red_or<1, 32 * CW>(!landed) : bar_red_or<2, 32 * CW>(!landed);
+      if (fail) {
+        timed_out = true;
+        break;
+      }
+    } else {
+      __syncwarp();
+    }
+    consumed = k + 1;
+    if (!F8 && cw == 0 && k + STAGES < n_mine) {
       issue(k + STAGES);
       ++issued;
     }
   }
 
   if (timed_out) {
-    // Drain this warp's copies still in flight (bounded) before giving up.
+    // Drain this warp's copies still in flight (bounded) before giving up
+    // (column warps other than the issuer have none).
     for (int k = consumed; k < issued; ++k)
       mbar_wait_bounded(bar0 + (k % STAGES) * 8, (k / STAGES) & 1, kWaitLimitNs);
     if (lane == 0) {
@@ -401,13 +424,13 @@ paged_decode_mma_kernel(const __grid_constant__ CUtensorMap tmK,
     return;
   }
 
-  constexpr int COLS = G::kCols;
+  constexpr int COLS = CCOLS;
   float* red_acc = reinterpret_cast<float*>(smem);
   float* red_m = red_acc + NW * COLS * (D + 4);
   float* red_l = red_m + NW * COLS;
   {
     float* base = red_acc + (warp * COLS) * (D + 4);
-    const int ca = (lane & 3) * 2;
+    const int ca = cw * G::kCols + (lane & 3) * 2;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int cc = nt * kMmaCols + ca;
@@ -963,12 +986,12 @@ static int choose_partition(int max_ctx, int BS, int rows_x_kvh, bool mma) {
 }
 
 
-template <typename T, bool QF32, int D, int BS, int NT, bool F8 = false>
+template <typename T, bool QF32, int D, int BS, int NT, bool F8 = false, int CW = 1>
 static int launch_mma(const DecodeArgs& a, const CUtensorMap& tk, const CUtensorMap& tv,
                       dim3 grid, cudaStream_t s) {
-  using G = MmaGeom<D, BS, NT, F8>;
+  using G = MmaGeom<D, BS, NT, F8, CW>;
   static uint64_t configured = 0;  // one bit per device ordinal
-  auto kern = paged_decode_mma_kernel<T, QF32, D, BS, NT, F8>;
+  auto kern = paged_decode_mma_kernel<T, QF32, D, BS, NT, F8, CW>;
   int dev = 0;
   int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   if (rc) return rc;
@@ -977,29 +1000,41 @@ static int launch_mma(const DecodeArgs& a, const CUtensorMap& tk, const CUtensor
     if (rc) return rc;
     if (dev < 64) configured |= 1ull << dev;
   }
-  return check_cuda(launch_pdl(kern, grid, dim3(kMmaThreads), G::kSmem, s, tk, tv, a),
+  return check_cuda(launch_pdl(kern, grid, dim3(G::kThreads), G::kSmem, s, tk, tv, a),
                     "paged_decode_mma launch");
 }
 
-template <typename T, bool QF32, int D, int NT>
+template <typename T, bool QF32, int D, int NT, int CW = 1>
 static int dispatch_bs(int BS, const DecodeArgs& a, const CUtensorMap& tk, const CUtensorMap& tv,
                        dim3 grid, cudaStream_t s) {
-  return BS == 16 ? launch_mma<T, QF32, D, 16, NT>(a, tk, tv, grid, s)
-                  : launch_mma<T, QF32, D, 32, NT>(a, tk, tv, grid, s);
+  return BS == 16 ? launch_mma<T, QF32, D, 16, NT, false, CW>(a, tk, tv, grid, s)
+                  : launch_mma<T, QF32, D, 32, NT, false, CW>(a, tk, tv, grid, s);
 }
 
-// 16-column CTAs (two n-tiles) exist for head_dim 64 and 128.
+// 16-column CTAs exist for head_dim 64 and 128: two column warps of one
+// n-tile per token warp (CLOVER_B200_COLSPLIT=0: one warp of two n-tiles).
+static bool colsplit_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("CLOVER_B200_COLSPLIT");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 template <typename T, bool QF32>
 static int dispatch_d(int D, int BS, const DecodeArgs& a, const CUtensorMap& tk,
                       const CUtensorMap& tv, dim3 grid, cudaStream_t s) {
   const bool wide = a.cols_per_cta > kMmaCols;
+  const bool split = colsplit_enabled();
   switch (D) {
     case 64:
-      return wide ? dispatch_bs<T, QF32, 64, 2>(BS, a, tk, tv, grid, s)
-                  : dispatch_bs<T, QF32, 64, 1>(BS, a, tk, tv, grid, s);
+      return !wide ? dispatch_bs<T, QF32, 64, 1>(BS, a, tk, tv, grid, s)
+             : split ? dispatch_bs<T, QF32, 64, 1, 2>(BS, a, tk, tv, grid, s)
+                     : dispatch_bs<T, QF32, 64, 2>(BS, a, tk, tv, grid, s);
     case 128:
-      return wide ? dispatch_bs<T, QF32, 128, 2>(BS, a, tk, tv, grid, s)
-                  : dispatch_bs<T, QF32, 128, 1>(BS, a, tk, tv, grid, s);
+      return !wide ? dispatch_bs<T, QF32, 128, 1>(BS, a, tk, tv, grid, s)
+             : split ? dispatch_bs<T, QF32, 128, 1, 2>(BS, a, tk, tv, grid, s)
+                     : dispatch_bs<T, QF32, 128, 2>(BS, a, tk, tv, grid, s);
     default: return dispatch_bs<T, QF32, 256, 1>(BS, a, tk, tv, grid, s);
   }
 }
