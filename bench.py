@@ -59,7 +59,7 @@ METRIC = "paged decode-attn KV-read GB/s"
 NCU_TRAFFIC = {
     ("c3", 1, "config"): (1.074150e9 + 9.415e6, "profiles/paged_decode_mma_c3_full.md"),
     ("c3", 8, "config"): (134.347e6 + 4.144e6, "profiles/paged_decode_mma_c3_shard8_full.md"),
-    ("c4", 1, "config"): (2.323797e9 + 27.557e6, "profiles/paged_decode_mma_c4_full.md"),
+    ("c4", 1, "config"): (2.324122e9 + 29.423e6, "profiles/paged_decode_mma_c4_full.md"),
 }
 
 
@@ -646,15 +646,26 @@ def run_e2e(cfg, lens, n_new, rank, world, device, args):
         qh = torch.randn((T, cfg.num_q_heads, D), generator=hg).pin_memory()
         kh = torch.randn((T, cfg.num_kv_heads, D), generator=hg).to(dt).pin_memory()
         vh = torch.randn((T, cfg.num_kv_heads, D), generator=hg).to(dt).pin_memory()
+        # Every rank holds the whole gathered output; the job reads it back
+        # once, each rank its own share of the rows.
+        r0, r1 = T * rank // world, T * (rank + 1) // world
+
         def call():
             # the output back into pinned host memory, then one stream sync
             out = be.decode_batch(ids, 0, qh, kh, vh, cfg.score_scale, n_new=n_new)
-            host = out.to("cpu", non_blocking=True)
+            host = out[r0:r1].to("cpu", non_blocking=True)
             torch.cuda.current_stream(device).synchronize()
             return host
     esz = torch.empty((), dtype=dt).element_size()
-    h2d = T * cfg.num_q_heads * D * 4 + 2 * T * cfg.num_kv_heads * D * esz
-    d2h = T * cfg.num_q_heads * D * 4
+    if single:
+        h2d = T * cfg.num_q_heads * D * 4 + 2 * T * cfg.num_kv_heads * D * esz
+        d2h = T * cfg.num_q_heads * D * 4
+    else:
+        # per rank: its heads of the inputs (decode_batch copies no others)
+        # and its share of the output rows
+        h2d = (T * cfg.num_q_heads * D * 4 + 2 * T * cfg.num_kv_heads * D * esz) * (hi - lo) \
+            // cfg.num_kv_heads
+        d2h = (r1 - r0) * cfg.num_q_heads * D * 4
     for _ in range(args.warmup):
         call()
     torch.cuda.synchronize(device)
@@ -678,6 +689,9 @@ def run_e2e(cfg, lens, n_new, rank, world, device, args):
     torch.cuda.empty_cache()
     return {"value": round(attended / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 5),
+            "bytes": "per rank" + ("" if single or world == 1 else
+                                   "; each rank copies its heads' inputs and reads 1/N of the "
+                                   "gathered output rows"),
             "api": ("B200AttentionBackend.decode_layer_batch (per-item host tensors)" if single
                     else "B200AttentionBackend.decode_batch (host tensors, multi-token)"),
             "gather": "none" if world == 1 else args.gather}

@@ -584,25 +584,46 @@ class B200AttentionBackend:
             raise ValueError(f"expected {T} new tokens, got q {tuple(query.shape)} k {tuple(key.shape)}")
         if self._pending_ingest:
             self._await_ingest()
-        dst = None if out is None else self._consumer_view(out, T, query.shape[1])
-        # host inputs start their (asynchronous, from pinned memory) copies now,
-        # so the planning below overlaps them
-        if not query.is_cuda:
-            query = query.to(self.device, non_blocking=True)
-        if not key.is_cuda:
-            key = key.to(self.device, non_blocking=True)
-        if not value.is_cuda:
-            value = value.to(self.device, non_blocking=True)
-        reqs, rows, targets, offs, ctx_rows = self._plan(request_ids, layer_idx, n_new, query.shape[1:])
+        hq = query.shape[1]
+        dst = None if out is None else self._consumer_view(out, T, hq)
+        q_shape = query.shape[1:]
+        # host inputs start their (asynchronous) copies now, so the planning
+        # below overlaps them; a sharded rank moves only its own heads
+        local = None
+        if not (query.is_cuda or key.is_cuda or value.is_cuda) and hq % self.num_kv_heads == 0:
+            lo, hi = self.kv_range
+            g = hq // self.num_kv_heads
+            query = self._h2d(query[:, lo * g:hi * g])
+            key = self._h2d(self._select_heads(key))
+            value = self._h2d(self._select_heads(value))
+            local = hq
+        else:
+            if not query.is_cuda:
+                query = query.to(self.device, non_blocking=True)
+            if not key.is_cuda:
+                key = key.to(self.device, non_blocking=True)
+            if not value.is_cuda:
+                value = value.to(self.device, non_blocking=True)
+        reqs, rows, targets, offs, ctx_rows = self._plan(request_ids, layer_idx, n_new, q_shape)
         meta = to_device_i32(rows + offs + ctx_rows, self.device)
         res = self._launch(reqs, layer_idx, n_new, targets, query, key, value, meta[0:B],
-                           meta[B:2 * B + 1], meta[2 * B + 1:], score_scale, dst=dst)
+                           meta[B:2 * B + 1], meta[2 * B + 1:], score_scale, dst=dst, hq=local)
         if dst is not None:
             if res.data_ptr() != dst.data_ptr():
                 dst.copy_(res)
             return dst
         # the fused gather's buffer is rewritten by the next call
         return res.clone() if self._peer is not None and res.data_ptr() == self._peer.out.data_ptr() else res
+
+    def _h2d(self, x: torch.Tensor) -> torch.Tensor:
+        """A host tensor on this backend's device, copied asynchronously: a
+        view of some heads (rows of contiguous values at a wider stride) goes
+        through a pinned staging copy, so only those bytes cross PCIe."""
+        if not x.is_contiguous():
+            stage = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+            stage.copy_(x)
+            x = stage
+        return x.to(self.device, non_blocking=True)
 
     def _consumer_view(self, out: torch.Tensor, T: int, hq: int) -> torch.Tensor:
         """[T, Hq, D] view of a consumer buffer whose T rows hold Hq * D values."""
@@ -648,33 +669,42 @@ class B200AttentionBackend:
         return reqs, rows, targets, offs, ctx_rows
 
     def _launch(self, reqs, layer_idx, n_new, targets, query, key, value, rows_d, offs_d, ctx_d,
-                score_scale, check: bool = True, pt: Optional[int] = None, dst=None):
+                score_scale, check: bool = True, pt: Optional[int] = None, dst=None,
+                hq: Optional[int] = None):
+        """``hq`` given: query, key and value are already this rank's heads on
+        the device (of ``hq`` query heads in all)."""
         pool = self.pool
         if pt is None:
             pt = self._split(targets, n_new)
-        hq = query.shape[1]
+        local = hq is not None
+        hq = query.shape[1] if hq is None else hq
         group = hq // self.num_kv_heads
         lo, hi = self.kv_range
         q = query.to(self.device, non_blocking=True)
         if q.dtype not in (torch.float32, self.kv_dtype):
             q = q.float()
-        if (lo, hi) != (0, self.num_kv_heads):
+        if not local and (lo, hi) != (0, self.num_kv_heads):
             q = q[:, lo * group:hi * group]
         if q.stride(2) != 1 or q.stride(1) != self.head_dim:
             q = q.contiguous()
+        if local:
+            k_loc = key.to(dtype=self.kv_dtype).contiguous()
+            v_loc = value.to(dtype=self.kv_dtype).contiguous()
+        else:
+            k_loc, v_loc = self._local_kv(key), self._local_kv(value)
         sharded = self.shard is not None and self.shard.world > 1
         peer = self._peer_for(q) if sharded else None
         if peer is not None:
             # fused append + decode + reduce with the all-gather over NVLink
-            out = pool.decode_step_gather(layer_idx, q, self._local_kv(key), self._local_kv(value),
-                                          offs_d, ctx_d, rows_d, max(n_new), max(targets),
-                                          score_scale, peer, partition_tokens=pt, out=dst)
+            out = pool.decode_step_gather(layer_idx, q, k_loc, v_loc, offs_d, ctx_d, rows_d,
+                                          max(n_new), max(targets), score_scale, peer,
+                                          partition_tokens=pt, out=dst)
         else:
             # one launch: append each row's token at ctx - 1, then attend (+ reduce)
             direct = dst is not None and not sharded and dst.dtype == q.dtype
-            out = pool.decode_step(layer_idx, q, self._local_kv(key), self._local_kv(value), offs_d,
-                                   ctx_d, rows_d, max(n_new), max(targets), score_scale,
-                                   out=dst if direct else None, partition_tokens=pt, check=check)
+            out = pool.decode_step(layer_idx, q, k_loc, v_loc, offs_d, ctx_d, rows_d, max(n_new),
+                                   max(targets), score_scale, out=dst if direct else None,
+                                   partition_tokens=pt, check=check)
         self._advance(reqs, layer_idx, n_new, targets)
         if sharded and peer is None:
             out = self.shard.gather(out, self.num_kv_heads, group)

@@ -791,15 +791,50 @@ static int launch_splitk_reduce(const DecodeArgs& a, int D, int n_rows, cudaStre
   return check_cuda(e, "splitk_reduce launch");
 }
 
+// One output value of a (row, head) with npp partials, by one thread: the
+// partials' log-sum-exp merge, online over batches of 8 partitions in flight.
+__device__ __forceinline__ float reduce_dim_serial(const DecodeArgs& a, int64_t base, int dim,
+                                                  int D, int npp) {
+  float m = -INFINITY, l = 0.f, o = 0.f;
+  for (int p0 = 0; p0 < npp; p0 += 8) {
+    float lv[8], ov[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const bool ok = p0 + i < npp;
+      lv[i] = ok ? __ldcg(a.part_lse + base + p0 + i) : -INFINITY;
+      ov[i] = ok ? __ldcg(a.part_out + (base + p0 + i) * D + dim) : 0.f;
+    }
+    float mm = m;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mm = fmaxf(mm, lv[i]);
+    const float u = mm == -INFINITY ? 0.f : mm;
+    const float sc = fast_exp2(m - u);
+    l *= sc;
+    o *= sc;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float e = fast_exp2(lv[i] - u);
+      l += e;
+      o = fmaf(e, ov[i], o);
+    }
+    m = mm;
+  }
+  return l > 0.f ? o / l : 0.f;
+}
+
 // Split-K reduce with the output all-gather fused in.  A unit is (query row,
-// local head, 32-dim chunk).  Phase 1: every CTA reduces its units (1 or more
-// partitions; 0 -> zeros) and stores each value, tagged with the epoch, into
-// EVERY rank's receive buffer over NVLink.  Phase 2: every CTA waits (bounded)
+// local head, 32-dim chunk) whose partitions the CTA's warps split, or, when
+// no unit has more than kGatherRowsMaxParts partials (ROWS), a whole (query
+// row, local head) with one thread per dim that merges the partials itself.
+// Phase 1: every CTA reduces its units (1 or more partitions; 0 -> zeros) and
+// stores each value, tagged with the epoch, into EVERY rank's receive buffer
+// over NVLink.  Phase 2: every CTA waits (bounded)
 // until its units' words from every rank carry the epoch and writes them to
 // the output [rows, total_q_heads, D] in place.  The grid never exceeds the
 // co-resident CTA count and each CTA sends before it waits, so no CTA can wait
 // on a CTA that has not started.
 constexpr int kGatherCtasPerSm = 4;
+constexpr int kGatherRowsMaxParts = 16;
 
 __device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -810,6 +845,7 @@ __device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
   return v;
 }
 
+template <bool ROWS>
 __global__ void __launch_bounds__(kReduceWarps * 32)
 reduce_gather_kernel(const DecodeArgs a, const GatherArgs g, int D) {
   __shared__ float s_m[kReduceWarps], s_l[kReduceWarps];
@@ -822,7 +858,8 @@ reduce_gather_kernel(const DecodeArgs a, const GatherArgs g, int D) {
   pdl_trigger();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t half = (int64_t)(epoch & 1) * g.ll_half_words;
-  const int dchunks = (D + kReduceDims - 1) / kReduceDims;
+  const int udims = ROWS ? D : kReduceDims;  // dims per unit
+  const int dchunks = (D + udims - 1) / udims;
   const int heads = a.num_q_heads;
 
   // ---- phase 1: reduce and send
@@ -830,13 +867,22 @@ reduce_gather_kernel(const DecodeArgs a, const GatherArgs g, int D) {
     const int dc = u % dchunks;
     const int h = (u / dchunks) % heads;
     const int r = u / (dchunks * heads);
-    const int dim = dc * kReduceDims + lane;
     const int npp = partial_count(a, r, h, __ldg(a.ctx + r));
-    const float v = reduce_unit<kGatherPartsPerWarp>(a, r, h, dim, D, npp, s_m, s_l, s_o);
-    if (warp == 0 && dim < D) {
-      const uint64_t word = ((uint64_t)(uint32_t)epoch << 32) | (uint64_t)__float_as_uint(v);
-      const int64_t idx = half + ((int64_t)r * g.total_q_heads + g.q_head_offset + h) * D + dim;
-      for (int rr = 0; rr < g.n_ranks; ++rr) st_relaxed_sys_u64(g.peer_ll[rr] + idx, word);
+    const int64_t orow = half + ((int64_t)r * g.total_q_heads + g.q_head_offset + h) * D;
+    if (ROWS) {
+      const int64_t base = ((int64_t)r * a.num_q_heads + h) * a.max_parts;
+      for (int dim = threadIdx.x; dim < D; dim += blockDim.x) {
+        const float v = reduce_dim_serial(a, base, dim, D, npp);
+        const uint64_t word = ((uint64_t)(uint32_t)epoch << 32) | (uint64_t)__float_as_uint(v);
+        for (int rr = 0; rr < g.n_ranks; ++rr) st_relaxed_sys_u64(g.peer_ll[rr] + orow + dim, word);
+      }
+    } else {
+      const int dim = dc * kReduceDims + lane;
+      const float v = reduce_unit<kGatherPartsPerWarp>(a, r, h, dim, D, npp, s_m, s_l, s_o);
+      if (warp == 0 && dim < D) {
+        const uint64_t word = ((uint64_t)(uint32_t)epoch << 32) | (uint64_t)__float_as_uint(v);
+        for (int rr = 0; rr < g.n_ranks; ++rr) st_relaxed_sys_u64(g.peer_ll[rr] + orow + dim, word);
+      }
     }
   }
 
@@ -847,9 +893,11 @@ reduce_gather_kernel(const DecodeArgs a, const GatherArgs g, int D) {
     const int dc = u % dchunks;
     const int h = (u / dchunks) % heads;
     const int r = u / (dchunks * heads);
-    const int dim = dc * kReduceDims + lane;
-    if (dim >= D) continue;
-    for (int rr = warp; rr < g.n_ranks; rr += kReduceWarps) {
+    const int d0 = dc * udims;
+    const int nd = min(udims, D - d0);
+    for (int i = threadIdx.x; i < g.n_ranks * nd; i += blockDim.x) {
+      const int rr = i / nd;
+      const int dim = d0 + (i - rr * nd);
       const int head = rr * heads + h;  // ranks hold equal, contiguous head ranges
       const uint64_t* src = g.peer_ll[g.rank] + half + ((int64_t)r * g.total_q_heads + head) * D + dim;
       uint64_t w = ld_relaxed_sys_u64(src);
@@ -1369,15 +1417,22 @@ static int decode_impl(
   if (rc) return rc;
   if (gather != nullptr) {
     GatherArgs g = *gather;
-    g.units = n_query_rows * num_q_heads * ((head_dim + kReduceDims - 1) / kReduceDims);
+    // Few partials per (row, head) (ragged and multi-token batches): a CTA
+    // per (row, head), a thread per dim.  Many (long contexts split over
+    // short partitions): 32-dim units whose partitions the warps split.
+    const bool rows = max_parts <= kGatherRowsMaxParts;
+    g.units = n_query_rows * num_q_heads * (rows ? 1 : (head_dim + kReduceDims - 1) / kReduceDims);
     int sms = 148;
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess)
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int grid = g.units < sms * kGatherCtasPerSm ? g.units : sms * kGatherCtasPerSm;
-    return check_cuda(launch_pdl(reduce_gather_kernel, dim3(grid), dim3(kReduceWarps * 32), 0, s,
-                                 a, g, head_dim),
-                      "reduce_gather launch");
+    const cudaError_t e =
+        rows ? launch_pdl(reduce_gather_kernel<true>, dim3(grid), dim3(kReduceWarps * 32), 0, s, a, g,
+                          head_dim)
+             : launch_pdl(reduce_gather_kernel<false>, dim3(grid), dim3(kReduceWarps * 32), 0, s, a,
+                          g, head_dim);
+    return check_cuda(e, "reduce_gather launch");
   }
   if (max_parts > 1 || pl.stream) {
     // Rows with several partitions are combined here; single-partition rows
