@@ -109,7 +109,8 @@ struct GatherArgs {
   int32_t* sync;             // this rank's sync words
   int32_t n_ranks, rank, q_head_offset, total_q_heads;
   int64_t ll_half_words;     // words per parity half (>= rows * total_q_heads * D)
-  int32_t units;             // rows * local heads * 32-dim chunks
+  int32_t units;             // reduce units: (row, local head[, 32-dim chunk])
+  int32_t rows;              // query rows of the step
 };
 
 struct ColInfo {

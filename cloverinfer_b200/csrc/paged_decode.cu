@@ -791,49 +791,9 @@ static int launch_splitk_reduce(const DecodeArgs& a, int D, int n_rows, cudaStre
   return check_cuda(e, "splitk_reduce launch");
 }
 
-// One output value of a (row, head) with npp partials, by one thread: the
-// partials' log-sum-exp merge, online over batches of 8 partitions in flight.
-__device__ __forceinline__ float reduce_dim_serial(const DecodeArgs& a, int64_t base, int dim,
-                                                  int D, int npp) {
-  float m = -INFINITY, l = 0.f, o = 0.f;
-  for (int p0 = 0; p0 < npp; p0 += 8) {
-    float lv[8], ov[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const bool ok = p0 + i < npp;
-      lv[i] = ok ? __ldcg(a.part_lse + base + p0 + i) : -INFINITY;
-      ov[i] = ok ? __ldcg(a.part_out + (base + p0 + i) * D + dim) : 0.f;
-    }
-    float mm = m;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) mm = fmaxf(mm, lv[i]);
-    const float u = mm == -INFINITY ? 0.f : mm;
-    const float sc = fast_exp2(m - u);
-    l *= sc;
-    o *= sc;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float e = fast_exp2(lv[i] - u);
-      l += e;
-      o = fmaf(e, ov[i], o);
-    }
-    m = mm;
-  }
-  return l > 0.f ? o / l : 0.f;
-}
-
-// Split-K reduce with the output all-gather fused in.  A unit is (query row,
-// local head, 32-dim chunk) whose partitions the CTA's warps split, or, when
-// no unit has more than kGatherRowsMaxParts partials (ROWS), a whole (query
-// row, local head) with one thread per dim that merges the partials itself.
-// Phase 1: every CTA reduces its units (1 or more partitions; 0 -> zeros) and
-// stores each value, tagged with the epoch, into EVERY rank's receive buffer
-// over NVLink.  Phase 2: every CTA waits (bounded)
-// until its units' words from every rank carry the epoch and writes them to
-// the output [rows, total_q_heads, D] in place.  The grid never exceeds the
-// co-resident CTA count and each CTA sends before it waits, so no CTA can wait
-// on a CTA that has not started.
 constexpr int kGatherCtasPerSm = 4;
+// (row, head) units of one warp when no pair has more partials than this,
+// or when the pairs alone fill the grid's warps.
 constexpr int kGatherRowsMaxParts = 16;
 
 __device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
@@ -845,7 +805,71 @@ __device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
   return v;
 }
 
-template <bool ROWS>
+// One (row, head) of the fused gather's reduce by one warp: lane l merges
+// dims l, l + 32, ... (EPL of them) over the partials, 8 partitions' loads
+// in flight, and sends each value, tagged with the epoch, to every rank.
+template <int EPL>
+__device__ __forceinline__ void gather_rows_unit(const DecodeArgs& a, const GatherArgs& g, int r,
+                                                 int h, int npp, int D, int64_t orow,
+                                                 uint32_t epoch, int lane) {
+  constexpr int PB = 8;
+  const int64_t base = ((int64_t)r * a.num_q_heads + h) * a.max_parts;
+  float m = -INFINITY, l = 0.f, o[EPL];
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) o[j] = 0.f;
+  for (int p0 = 0; p0 < npp; p0 += PB) {
+    float lv[PB], ov[PB][EPL];
+#pragma unroll
+    for (int i = 0; i < PB; ++i) {
+      const bool ok = p0 + i < npp;
+      lv[i] = ok ? __ldcg(a.part_lse + base + p0 + i) : -INFINITY;
+#pragma unroll
+      for (int j = 0; j < EPL; ++j) {
+        const int d = lane + 32 * j;
+        ov[i][j] = (ok && d < D) ? __ldcg(a.part_out + (base + p0 + i) * D + d) : 0.f;
+      }
+    }
+    float mm = m;
+#pragma unroll
+    for (int i = 0; i < PB; ++i) mm = fmaxf(mm, lv[i]);
+    const float u = mm == -INFINITY ? 0.f : mm;
+    const float sc = fast_exp2(m - u);
+    l *= sc;
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) o[j] *= sc;
+#pragma unroll
+    for (int i = 0; i < PB; ++i) {
+      const float e = fast_exp2(lv[i] - u);
+      l += e;
+#pragma unroll
+      for (int j = 0; j < EPL; ++j) o[j] = fmaf(e, ov[i][j], o[j]);
+    }
+    m = mm;
+  }
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int d = lane + 32 * j;
+    if (d >= D) continue;
+    const float v = l > 0.f ? o[j] / l : 0.f;
+    const uint64_t word = ((uint64_t)epoch << 32) | (uint64_t)__float_as_uint(v);
+    for (int rr = 0; rr < g.n_ranks; ++rr) st_relaxed_sys_u64(g.peer_ll[rr] + orow + d, word);
+  }
+}
+
+// Split-K reduce with the output all-gather fused in.
+// Phase 1: every CTA reduces its units (1 or more partitions; 0 -> zeros) and
+// stores each value, tagged with the epoch, into EVERY rank's receive buffer
+// over NVLink.  A unit is either (EPL = 0) a (query row, local head, 32-dim
+// chunk) whose partitions the CTA's warps split — few (row, head) pairs with
+// many partials each — or (EPL > 0) a whole (query row, local head) that one
+// warp merges, EPL dims per lane — many pairs with few partials each.
+// Phase 2: the grid's threads share out every word of the receive buffer
+// (all ranks' heads of all rows), 8 loads in flight per thread, wait
+// (bounded) until each carries the epoch and write it to the output
+// [rows, total_q_heads, D] in place.  The grid never exceeds the co-resident
+// CTA count and each CTA sends before it waits, so no CTA can wait on a CTA
+// that has not started.
+template <int EPL>
 __global__ void __launch_bounds__(kReduceWarps * 32)
 reduce_gather_kernel(const DecodeArgs a, const GatherArgs g, int D) {
   __shared__ float s_m[kReduceWarps], s_l[kReduceWarps];
@@ -858,59 +882,65 @@ reduce_gather_kernel(const DecodeArgs a, const GatherArgs g, int D) {
   pdl_trigger();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t half = (int64_t)(epoch & 1) * g.ll_half_words;
-  const int udims = ROWS ? D : kReduceDims;  // dims per unit
-  const int dchunks = (D + udims - 1) / udims;
   const int heads = a.num_q_heads;
 
   // ---- phase 1: reduce and send
-  for (int u = blockIdx.x; u < g.units; u += gridDim.x) {
-    const int dc = u % dchunks;
-    const int h = (u / dchunks) % heads;
-    const int r = u / (dchunks * heads);
-    const int npp = partial_count(a, r, h, __ldg(a.ctx + r));
-    const int64_t orow = half + ((int64_t)r * g.total_q_heads + g.q_head_offset + h) * D;
-    if (ROWS) {
-      const int64_t base = ((int64_t)r * a.num_q_heads + h) * a.max_parts;
-      for (int dim = threadIdx.x; dim < D; dim += blockDim.x) {
-        const float v = reduce_dim_serial(a, base, dim, D, npp);
-        const uint64_t word = ((uint64_t)(uint32_t)epoch << 32) | (uint64_t)__float_as_uint(v);
-        for (int rr = 0; rr < g.n_ranks; ++rr) st_relaxed_sys_u64(g.peer_ll[rr] + orow + dim, word);
-      }
-    } else {
+  if (EPL > 0) {
+    for (int u = blockIdx.x * kReduceWarps + warp; u < g.units; u += gridDim.x * kReduceWarps) {
+      const int h = u % heads, r = u / heads;
+      const int npp = partial_count(a, r, h, __ldg(a.ctx + r));
+      const int64_t orow = half + ((int64_t)r * g.total_q_heads + g.q_head_offset + h) * D;
+      gather_rows_unit<(EPL > 0 ? EPL : 1)>(a, g, r, h, npp, D, orow, (uint32_t)epoch, lane);
+    }
+  } else {
+    const int dchunks = (D + kReduceDims - 1) / kReduceDims;
+    for (int u = blockIdx.x; u < g.units; u += gridDim.x) {
+      const int dc = u % dchunks;
+      const int h = (u / dchunks) % heads;
+      const int r = u / (dchunks * heads);
       const int dim = dc * kReduceDims + lane;
+      const int npp = partial_count(a, r, h, __ldg(a.ctx + r));
       const float v = reduce_unit<kGatherPartsPerWarp>(a, r, h, dim, D, npp, s_m, s_l, s_o);
       if (warp == 0 && dim < D) {
         const uint64_t word = ((uint64_t)(uint32_t)epoch << 32) | (uint64_t)__float_as_uint(v);
-        for (int rr = 0; rr < g.n_ranks; ++rr) st_relaxed_sys_u64(g.peer_ll[rr] + orow + dim, word);
+        const int64_t idx = half + ((int64_t)r * g.total_q_heads + g.q_head_offset + h) * D + dim;
+        for (int rr = 0; rr < g.n_ranks; ++rr) st_relaxed_sys_u64(g.peer_ll[rr] + idx, word);
       }
     }
   }
 
-  // ---- phase 2: receive every rank's words for this CTA's units
+  // ---- phase 2: receive every word of the buffer (all ranks' heads)
   bool timed_out = false;
   const uint64_t t0 = global_timer_ns();
-  for (int u = blockIdx.x; u < g.units; u += gridDim.x) {
-    const int dc = u % dchunks;
-    const int h = (u / dchunks) % heads;
-    const int r = u / (dchunks * heads);
-    const int d0 = dc * udims;
-    const int nd = min(udims, D - d0);
-    for (int i = threadIdx.x; i < g.n_ranks * nd; i += blockDim.x) {
-      const int rr = i / nd;
-      const int dim = d0 + (i - rr * nd);
-      const int head = rr * heads + h;  // ranks hold equal, contiguous head ranges
-      const uint64_t* src = g.peer_ll[g.rank] + half + ((int64_t)r * g.total_q_heads + head) * D + dim;
-      uint64_t w = ld_relaxed_sys_u64(src);
-      while ((uint32_t)(w >> 32) != (uint32_t)epoch && !timed_out) {
+  const int64_t n_words = (int64_t)g.rows * g.total_q_heads * D;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const uint64_t* rb = g.peer_ll[g.rank] + half;
+  constexpr int kInFlight = 8;
+  for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < n_words;
+       i0 += kInFlight * stride) {
+    uint64_t w[kInFlight];
+#pragma unroll
+    for (int k = 0; k < kInFlight; ++k) {
+      const int64_t i = i0 + k * stride;
+      w[k] = i < n_words ? ld_relaxed_sys_u64(rb + i) : 0;
+    }
+#pragma unroll
+    for (int k = 0; k < kInFlight; ++k) {
+      const int64_t i = i0 + k * stride;
+      if (i >= n_words) break;
+      while ((uint32_t)(w[k] >> 32) != (uint32_t)epoch && !timed_out) {
         if (global_timer_ns() - t0 > a.wait_ns) {
           timed_out = true;
           break;
         }
-        w = ld_relaxed_sys_u64(src);
+        w[k] = ld_relaxed_sys_u64(rb + i);
       }
-      const float v = __uint_as_float((uint32_t)w);
-      const int64_t oidx = (int64_t)r * a.out_stride + (int64_t)head * D + dim;
-      store_out(a, oidx, timed_out ? 0.f : v);
+      const int64_t rh = i / D;
+      const int dim = (int)(i - rh * D);
+      const int64_t r = rh / g.total_q_heads;
+      const int head = (int)(rh - r * g.total_q_heads);
+      store_out(a, r * a.out_stride + (int64_t)head * D + dim,
+                timed_out ? 0.f : __uint_as_float((uint32_t)w[k]));
     }
   }
   if (timed_out) raise_status(a.status, CLOVER_B200_DEV_TIMEOUT);
@@ -1417,22 +1447,40 @@ static int decode_impl(
   if (rc) return rc;
   if (gather != nullptr) {
     GatherArgs g = *gather;
-    // Few partials per (row, head) (ragged and multi-token batches): a CTA
-    // per (row, head), a thread per dim.  Many (long contexts split over
-    // short partitions): 32-dim units whose partitions the warps split.
-    const bool rows = max_parts <= kGatherRowsMaxParts;
-    g.units = n_query_rows * num_q_heads * (rows ? 1 : (head_dim + kReduceDims - 1) / kReduceDims);
     int sms = 148;
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess)
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int grid = g.units < sms * kGatherCtasPerSm ? g.units : sms * kGatherCtasPerSm;
-    const cudaError_t e =
-        rows ? launch_pdl(reduce_gather_kernel<true>, dim3(grid), dim3(kReduceWarps * 32), 0, s, a, g,
-                          head_dim)
-             : launch_pdl(reduce_gather_kernel<false>, dim3(grid), dim3(kReduceWarps * 32), 0, s, a,
-                          g, head_dim);
-    return check_cuda(e, "reduce_gather launch");
+    // Many (row, head) pairs, or few partials each (ragged and multi-token
+    // batches): a warp per pair.  Few pairs with many partials each (long
+    // contexts over short partitions): 32-dim units whose partitions the
+    // CTA's warps split.
+    const int64_t pairs = (int64_t)n_query_rows * num_q_heads;
+    const bool rows = max_parts <= kGatherRowsMaxParts ||
+                      pairs >= (int64_t)sms * kGatherCtasPerSm * kReduceWarps;
+    const int64_t units = rows ? pairs : pairs * ((head_dim + kReduceDims - 1) / kReduceDims);
+    if (units > INT32_MAX) return set_error(CLOVER_B200_ERR_UNSUPPORTED, "reduce_gather: too many rows");
+    g.units = (int)units;
+    g.rows = n_query_rows;
+    const int epl = (head_dim + 31) / 32;
+    auto kern = !rows ? reduce_gather_kernel<0>
+                : epl <= 1 ? reduce_gather_kernel<1>
+                : epl <= 2 ? reduce_gather_kernel<2>
+                : epl <= 4 ? reduce_gather_kernel<4>
+                           : reduce_gather_kernel<8>;
+    // Every CTA waits for words that any CTA of any rank sends: the whole
+    // grid must be resident at once (at most kGatherCtasPerSm per SM, and
+    // no more than the kernel's registers allow).
+    int per_sm = 0;
+    rc = check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kReduceWarps * 32, 0),
+                    "reduce_gather occupancy");
+    if (rc) return rc;
+    if (per_sm <= 0) return set_error(CLOVER_B200_ERR_UNSUPPORTED, "reduce_gather: no resident CTA");
+    const int64_t cap = (int64_t)sms * (per_sm < kGatherCtasPerSm ? per_sm : kGatherCtasPerSm);
+    const int64_t want = rows ? (units + kReduceWarps - 1) / kReduceWarps : units;
+    const int grid = (int)(want < cap ? (want > 0 ? want : 1) : cap);
+    return check_cuda(launch_pdl(kern, dim3(grid), dim3(kReduceWarps * 32), 0, s, a, g, head_dim),
+                      "reduce_gather launch");
   }
   if (max_parts > 1 || pl.stream) {
     // Rows with several partitions are combined here; single-partition rows
@@ -1517,6 +1565,7 @@ static int step_gather_impl(
   g.total_q_heads = (int32_t)total_q_heads;
   g.ll_half_words = recv_half_words;
   g.units = 0;
+  g.rows = 0;
   return decode_impl(out, out_row_stride, q, q_row_stride, q_dtype, k_cache, v_cache, kv_dtype,
                      num_blocks, block_size, k_new, v_new, new_token_stride, block_tables,
                      table_stride, seq_rows, query_start_loc, ctx_lens, n_seqs, n_query_rows,

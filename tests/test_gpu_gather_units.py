@@ -1,11 +1,11 @@
 """Both unit shapes of the fused gather's split-K reduce, on one GPU.
 
 ``clover_b200_decode_step_gather`` merges the decode's partials and sends each
-value to every rank.  When no (row, head) has more than 16 partials it takes
-one (row, head) per CTA with a thread per dim; otherwise 32-dim units whose
-partitions the CTA's warps split.  A one-rank gather (its own receive buffer
-only) runs the whole kernel, sends and bounded receives included, with no
-peer: here a ragged multi-token GQA batch at two partition lengths, one per
+value to every rank.  When no (row, head) has more than 16 partials (or the
+pairs alone fill the grid's warps) a warp takes a whole (row, head);
+otherwise 32-dim units whose partitions the CTA's warps split.  A one-rank
+gather (its own receive buffer only) runs the whole kernel, sends and bounded
+receives included, with no peer: here a ragged multi-token GQA batch at two partition lengths, one per
 unit shape, is held to the CPU oracle (``oracle.attend`` over the sequence's
 blocks, each row with its causal limit).
 """
