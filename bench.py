@@ -426,7 +426,25 @@ def run_b200(args):
     st = build_step(cfg, rank, world, lens, device, gather=peer, n_new=n_new, partition_tokens=pt_arg)
     st["peer"] = peer
     local_kv = kv_bytes(lens, st["hkv_local"], cfg.head_dim, cfg.dtype)
-    full_step, gathered = _step_runner(st, world, T, cfg, device)
+    # A step whose KV fits twice in L2 (C1, C2) would find it there on the
+    # next step: the timed steps then rotate over independent copies of the
+    # workload (own pool, tables and buffers), more than 2 x L2 in all.
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    n_copies = min(64, max(1, -(-2 * l2 // max(local_kv, 1)) + 1)) if local_kv < 2 * l2 else 1
+    copies = [st] + [dict(build_step(cfg, rank, world, lens, device, seed=c, gather=peer, n_new=n_new,
+                                     partition_tokens=pt_arg), peer=peer) for c in range(1, n_copies)]
+    runners = [_step_runner(c, world, T, cfg, device) for c in copies]
+    full_step, gathered = runners[0]
+    rot = {"i": 0}
+
+    def step_rot():
+        # the next copy's step (the order is fixed when a graph captures it)
+        runners[rot["i"] % n_copies][0]()
+        rot["i"] += 1
+
+    def decode_rot():
+        copies[rot["i"] % n_copies]["decode_only"]()
+        rot["i"] += 1
 
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
@@ -435,13 +453,15 @@ def run_b200(args):
 
     with torch.cuda.stream(stream):
         for _ in range(3):  # eager warm-up (module load, tensor maps, NCCL comm init)
-            full_step()
+            for run, _ in runners:
+                run()
     torch.cuda.synchronize(device)
     # K timed steps back to back in one CUDA graph: one graph launch per K
     # steps, and programmatic dependent launch between a step's reduce and the
     # next step's decode.  The warm-up replays the same graph (its first launch
     # also uploads it), so at least W steps run untimed.
-    graph = None if args.no_graph else _capture(full_step, args.steps, stream)
+    rot["i"] = 0
+    graph = None if args.no_graph else _capture(step_rot, args.steps, stream)
     warm_replays = -(-args.warmup // args.steps)
     warm_steps = warm_replays * args.steps if graph is not None else args.warmup
 
@@ -450,13 +470,14 @@ def run_b200(args):
             graph.replay()
         else:
             for _ in range(n):
-                full_step()
+                step_rot()
 
     with torch.cuda.stream(stream):
         for _ in range(warm_replays if graph is not None else 1):
             run_steps(args.warmup)
     torch.cuda.synchronize(device)
-    st["pool"].check_status()
+    for c in copies:
+        c["pool"].check_status()
 
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     clocks = ClockSampler(vis.split(",")[local] if vis else str(local))
@@ -489,14 +510,16 @@ def run_b200(args):
     # Dominant kernel alone: decode (+ its split-K reduce) launches back to back
     # in one graph, timed between CUDA events on the launching stream (median
     # of the individually timed replays).
-    dec_graph = _capture(st["decode_only"], args.steps, stream)
+    rot["i"] = 0
+    dec_graph = _capture(decode_rot, args.steps, stream)
     with torch.cuda.stream(stream):
         dec_graph.replay()
     torch.cuda.synchronize(device)
     dec_reps = _replay_ms(dec_graph, stream, args.replays, args.steps)
     dec_ms = statistics.median(dec_reps)
     clk = clocks.stop()
-    st["pool"].check_status()
+    for c in copies:
+        c["pool"].check_status()
     used_graph = graph is not None
     # Release every graph (one may hold NCCL work) before anything else: a
     # live graph with NCCL calls makes destroy_process_group wait for good.
@@ -567,7 +590,10 @@ def run_b200(args):
                    "parallelism": f"kv-head-shard{world}", "gather": gather_kind,
                    "cuda_graph": ("%d steps per graph" % args.steps) if used_graph else "none",
                    "warmup_steps_run": warm_steps,
-                   "l2": "inputs > L2 (KV %.0f MB per GPU)" % (local_kv / 1e6)},
+                   "l2": ("inputs > L2 (KV %.0f MB per GPU)" % (local_kv / 1e6)) if n_copies == 1 else
+                         ("KV %.1f MB per GPU < 2 x L2 (%.0f MB): the timed steps rotate over %d independent "
+                          "copies of the workload (%.0f MB in all)"
+                          % (local_kv / 1e6, l2 / 1e6, n_copies, n_copies * local_kv / 1e6))},
         "steps_per_s": round(1e3 / ms, 2),
         "tokens_per_s": round(T * 1e3 / ms, 2),
         "pct_hbm_peak_per_gpu": round(100.0 * value / world / hbm_peak, 2),
