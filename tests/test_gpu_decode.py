@@ -251,3 +251,38 @@ def test_backend_interface_semantics():
     with pytest.raises(KeyError):
         be.get_context_len("r")
     assert be.pool.free_count == 64
+
+
+# ---------------------------------------------------------------- host inputs
+@pytest.mark.parametrize("form", ["pinned", "pageable", "expanded-kv"])
+def test_decode_batch_host_inputs_match_device_inputs(form):
+    """decode_batch with host tensors (copied asynchronously, through a
+    pinned staging copy where the heads it keeps are not contiguous) gives
+    exactly what the same call with device tensors gives."""
+    hkv, grp, D, bs = 2, 4, 128, 16
+    hq = hkv * grp
+    lens, n_new = [300, 17, 1000], [2, 1, 3]
+    g = torch.Generator().manual_seed(21)
+    bes = [_backend(num_blocks=256, block_size=bs, num_kv_heads=hkv, max_seqs=4, shuffle_seed=3)
+           for _ in range(2)]
+    ids = [f"h{i}" for i in range(len(lens))]
+    for rid, n in zip(ids, lens):
+        kv = [{"key": torch.randn(n, hkv, D, generator=g).bfloat16(),
+               "value": torch.randn(n, hkv, D, generator=g).bfloat16()}]
+        for be in bes:
+            be.init_request(rid, kv)
+    T = sum(n_new)
+    for step in range(2):
+        q = torch.randn(T, hq, D, generator=g).bfloat16().float()
+        k = torch.randn(T, hkv, D, generator=g).bfloat16()
+        v = torch.randn(T, hkv, D, generator=g).bfloat16()
+        ref = bes[0].decode_batch(ids, 0, q.cuda(), k.cuda(), v.cuda(), 1 / math.sqrt(D),
+                                  n_new=n_new).cpu()
+        if form == "expanded-kv":
+            k, v = repeat_kv(k, grp), repeat_kv(v, grp)
+        if form != "pageable":
+            q, k, v = q.pin_memory(), k.pin_memory(), v.pin_memory()
+        out = bes[1].decode_batch(ids, 0, q, k, v, 1 / math.sqrt(D), n_new=n_new)
+        assert out.is_cuda and out.shape == (T, hq, D)
+        assert torch.equal(out.cpu(), ref), f"{form}, step {step}"
+        assert [bes[1].get_context_len(r) for r in ids] == [bes[0].get_context_len(r) for r in ids]
