@@ -232,6 +232,16 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------ B200 arm
+def l2_copies(kv_bytes_per_step: int, l2_bytes: int) -> int:
+    """Independent copies of a workload the timed steps rotate over: 1 when a
+    step's KV is at least twice the L2, else enough that the copies together
+    exceed twice the L2 with one to spare (at most 64), so the KV a step
+    reads was last touched more than 2 x L2 bytes earlier."""
+    if kv_bytes_per_step >= 2 * l2_bytes:
+        return 1
+    return min(64, -(-2 * l2_bytes // max(kv_bytes_per_step, 1)) + 1)
+
+
 def build_step(cfg, rank, world, lens, device, seed=0, gather=None, n_new=None, partition_tokens=0):
     from cloverinfer_b200.workloads import build_decode_step
     return build_decode_step(cfg, rank, world, lens, device, seed=seed, gather=gather, n_new=n_new,
@@ -430,7 +440,7 @@ def run_b200(args):
     # next step: the timed steps then rotate over independent copies of the
     # workload (own pool, tables and buffers), more than 2 x L2 in all.
     l2 = torch.cuda.get_device_properties(device).L2_cache_size
-    n_copies = min(64, max(1, -(-2 * l2 // max(local_kv, 1)) + 1)) if local_kv < 2 * l2 else 1
+    n_copies = l2_copies(local_kv, l2)
     copies = [st] + [dict(build_step(cfg, rank, world, lens, device, seed=c, gather=peer, n_new=n_new,
                                      partition_tokens=pt_arg), peer=peer) for c in range(1, n_copies)]
     runners = [_step_runner(c, world, T, cfg, device) for c in copies]

@@ -90,3 +90,16 @@ def test_check_parity_passes_and_flags():
     res = bench.check_parity(cfg, st, lens, 1, torch.device("cpu"), want)
     assert res["append_mismatches"] == 1 and not res["pass"]
     assert math.isclose(res["tolerance"]["max_abs"], 2e-3)
+
+
+def test_l2_copies_rule():
+    l2 = 132_644_864  # B200: 126.5 MiB
+    assert bench.l2_copies(1_073_741_824, l2) == 1            # C3 on one GPU
+    assert bench.l2_copies(2 * l2, l2) == 1
+    assert bench.l2_copies(134_217_728, l2) == 3               # one rank's C3 share at 8 GPUs
+    assert bench.l2_copies(165_150_720, l2) == 3               # C2
+    assert bench.l2_copies(8_000_000, l2) == 35                # C1
+    assert bench.l2_copies(1, l2) == 64
+    for kv in (10_000_000, 100_000_000, 200_000_000):
+        n = bench.l2_copies(kv, l2)
+        assert (n - 1) * kv >= 2 * l2 or n == 64  # the others fill 2 x L2 between reuses
