@@ -573,6 +573,7 @@ def run_b200(args):
         par2 = check_parity(cfg, st2, lens, world, device, gathered2())
         med2 = statistics.median(reps2)
         as_cfg = {"partition_tokens": st2["partition_tokens"],
+                  "l2": "one copy of the workload (KV %.0f MB per GPU)" % (local_kv / 1e6),
                   "value": round(total_kv / (med2 * 1e-3) / 1e9, 2), "unit": "GB/s",
                   "ms_per_step": round(med2, 5), "spread": _spread(reps2),
                   "parity": {k: par2[k] for k in ("max_abs", "max_rel", "pass")}}
