@@ -44,6 +44,7 @@ from typing import Dict, List, Optional, Sequence
 import torch
 
 from . import _lib
+from .head_groups import local_inputs, select_kv_heads
 from .kv_cache import PagedKVPool, auto_partition, to_device_i32
 
 
@@ -220,15 +221,7 @@ class B200AttentionBackend:
     def _select_heads(self, x: torch.Tensor) -> torch.Tensor:
         """View of [T, H, D] with this rank's KV heads only.  H may be Hkv
         (native) or Hq = Hkv * g (repeat_kv-expanded: one head per group kept)."""
-        h = x.shape[1]
-        if h != self.num_kv_heads:
-            if h % self.num_kv_heads:
-                raise ValueError(f"K/V has {h} heads; expected {self.num_kv_heads} (or a multiple)")
-            x = x[:, :: h // self.num_kv_heads]
-        lo, hi = self.kv_range
-        if (lo, hi) != (0, self.num_kv_heads):
-            x = x[:, lo:hi]
-        return x
+        return select_kv_heads(x, self.kv_range, self.num_kv_heads)
 
     def _local_kv(self, x: torch.Tensor) -> torch.Tensor:
         """[T, H, D] on device in the cache dtype, local KV heads only."""
@@ -591,11 +584,8 @@ class B200AttentionBackend:
         # below overlaps them; a sharded rank moves only its own heads
         local = None
         if not (query.is_cuda or key.is_cuda or value.is_cuda) and hq % self.num_kv_heads == 0:
-            lo, hi = self.kv_range
-            g = hq // self.num_kv_heads
-            query = self._h2d(query[:, lo * g:hi * g])
-            key = self._h2d(self._select_heads(key))
-            value = self._h2d(self._select_heads(value))
+            query, key, value = (self._h2d(x) for x in
+                                 local_inputs(query, key, value, self.kv_range, self.num_kv_heads))
             local = hq
         else:
             if not query.is_cuda:

@@ -123,3 +123,29 @@ def kv_head_shards(num_kv_heads: int, world: int) -> List[Tuple[int, int]]:
     if world > num_kv_heads:
         raise ValueError(f"cannot shard {num_kv_heads} KV heads over {world} ranks")
     return group_ranges("balanced", num_kv_heads, world)
+
+
+def select_kv_heads(x, kv_range: Tuple[int, int], num_kv_heads: int):
+    """View of K or V [T, H, D] with KV heads [lo, hi) only.  H may be Hkv
+    (native) or Hq = Hkv * g (repeat_kv-expanded, model_adapter.py:504-507:
+    one head per group kept)."""
+    h = x.shape[1]
+    if h != num_kv_heads:
+        if h % num_kv_heads:
+            raise ValueError(f"K/V has {h} heads; expected {num_kv_heads} (or a multiple)")
+        x = x[:, :: h // num_kv_heads]
+    lo, hi = kv_range
+    return x if (lo, hi) == (0, num_kv_heads) else x[:, lo:hi]
+
+
+def local_inputs(query, key, value, kv_range: Tuple[int, int], num_kv_heads: int):
+    """A sharded rank's part of a step's inputs, as views: the query heads of
+    KV heads [lo, hi) (each KV head's GQA group is contiguous in query
+    [T, Hq, D]) and those KV heads of key/value."""
+    hq = query.shape[1]
+    if hq % num_kv_heads:
+        raise ValueError(f"{hq} query heads do not fit {num_kv_heads} KV heads")
+    g = hq // num_kv_heads
+    lo, hi = kv_range
+    q = query if (lo, hi) == (0, num_kv_heads) else query[:, lo * g:hi * g]
+    return q, select_kv_heads(key, kv_range, num_kv_heads), select_kv_heads(value, kv_range, num_kv_heads)

@@ -40,3 +40,38 @@ def test_kv_head_shards():
     with pytest.raises(ValueError):
         kv_head_shards(4, 8)
     assert group_ranges("legacy", 7, 3) == [(0, 3), (3, 6), (6, 7)]
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_local_inputs_partition_every_head(world):
+    """Each rank's part of a step's inputs (what a sharded decode_batch copies
+    from host memory): the query heads of its KV heads, and those KV heads of
+    native or repeat_kv-expanded K/V; the parts cover every head once."""
+    import torch
+    from cloverinfer_b200.head_groups import kv_head_shards, local_inputs
+    T, hkv, g, D = 5, 8, 4, 16
+    q = torch.randn(T, hkv * g, D)
+    k = torch.randn(T, hkv, D)
+    v = torch.randn(T, hkv, D)
+    k_exp = k.repeat_interleave(g, dim=1)  # repeat_kv: each KV head repeated g times in place
+    qs, ks, vs = [], [], []
+    for lo, hi in kv_head_shards(hkv, world):
+        ql, kl, vl = local_inputs(q, k, v, (lo, hi), hkv)
+        _, kx, vx = local_inputs(q, k_exp, v.repeat_interleave(g, dim=1), (lo, hi), hkv)
+        assert ql.shape == (T, (hi - lo) * g, D) and kl.shape == (T, hi - lo, D)
+        assert torch.equal(kx, kl) and torch.equal(vx, vl)
+        assert ql.data_ptr() >= q.data_ptr()  # views, no copies
+        qs.append(ql)
+        ks.append(kl)
+        vs.append(vl)
+    assert torch.equal(torch.cat(qs, 1), q) and torch.equal(torch.cat(ks, 1), k)
+    assert torch.equal(torch.cat(vs, 1), v)
+
+
+def test_local_inputs_reject_bad_head_counts():
+    import torch
+    from cloverinfer_b200.head_groups import local_inputs
+    with pytest.raises(ValueError):
+        local_inputs(torch.zeros(1, 6, 4), torch.zeros(1, 4, 4), torch.zeros(1, 4, 4), (0, 4), 4)
+    with pytest.raises(ValueError):
+        local_inputs(torch.zeros(1, 8, 4), torch.zeros(1, 6, 4), torch.zeros(1, 6, 4), (0, 4), 4)
